@@ -1,0 +1,153 @@
+/*
+ * mla_b200.h — C-ABI of the B200-native absorbed Multi-head Latent Attention
+ * (MLA) decode layer-forward.
+ *
+ * The reference project (pgangwar-ucsd/mla-cuda) exposes this path as the
+ * pybind11 module `mla_custom_cuda` with two functions:
+ *
+ *   q_absorbed(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim, rope_dim, eps)
+ *       -> [q_absorbed, q_rope]            (mla_kernels.cu:599-608, bound at :1689-1690)
+ *   mla_attention(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale) -> out
+ *                                          (mla_kernels.cu:1479-1485, bound at :1691-1692)
+ *
+ * This header is the C boundary beneath the drop-in replacement of that module.
+ * Every entry point takes raw device pointers to contiguous row-major arrays,
+ * 64-bit sizes, a caller-owned workspace and a CUDA stream passed as `void*`
+ * (a `cudaStream_t`; NULL is the legacy default stream). Nothing here
+ * allocates device memory or synchronises the device: all work is enqueued on
+ * the given stream, as the reference enqueues on the current torch stream
+ * (mla_kernels.cu:667, :1549).
+ *
+ * Errors are returned as `mla_status_t`; `mla_last_error_message()` gives a
+ * human-readable description of the most recent failure on the calling thread.
+ * The Python shim turns any non-zero status into `RuntimeError`, which is what
+ * the reference's TORCH_CHECK raises (mla_kernels.cu:627-635).
+ */
+#ifndef MLA_B200_H_
+#define MLA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MLA_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MLA_API __attribute__((visibility("default")))
+#else
+#define MLA_API
+#endif
+
+typedef enum mla_status {
+    MLA_OK = 0,
+    MLA_ERR_INVALID_ARGUMENT = 1, /* bad shape, null pointer or inconsistent sizes   */
+    MLA_ERR_UNSUPPORTED = 2,      /* dtype / precision / shape combination not built */
+    MLA_ERR_WORKSPACE = 3,        /* workspace pointer null or smaller than required */
+    MLA_ERR_CUDA = 4              /* a CUDA runtime call or kernel launch failed     */
+} mla_status_t;
+
+/* Storage dtype of every floating-point operand and output of one call. The
+ * reference dispatches fp32/fp64/fp16 (AT_DISPATCH_FLOATING_TYPES_AND_HALF,
+ * mla_kernels.cu:674, :1561); bf16 is new here. */
+typedef enum mla_dtype {
+    MLA_DTYPE_F32 = 0,
+    MLA_DTYPE_F64 = 1,
+    MLA_DTYPE_F16 = 2,
+    MLA_DTYPE_BF16 = 3
+} mla_dtype_t;
+
+/* Arithmetic used by a call.
+ *  MLA_PREC_EXACT : every product and sum in the accumulate dtype (fp64 for
+ *                   fp64 storage, fp32 otherwise), the reference's policy
+ *                   (AccType, mla_kernels.cu:118-120). rel-L2 <= 1e-5 in fp32.
+ *  MLA_PREC_TENSOR: tcgen05 tensor cores with bf16 operands and fp32
+ *                   accumulation, scores never written to memory. fp32, fp16
+ *                   and bf16 storage; rel-L2 <= 2e-2 against the fp32 path. */
+typedef enum mla_precision {
+    MLA_PREC_EXACT = 0,
+    MLA_PREC_TENSOR = 1
+} mla_precision_t;
+
+/* ABI version of the loaded library (MLA_B200_ABI_VERSION at build time). */
+MLA_API int mla_abi_version(void);
+
+/* Static description of a status code. */
+MLA_API const char* mla_status_string(mla_status_t status);
+
+/* Message of the last failed call on this thread ("" if none). */
+MLA_API const char* mla_last_error_message(void);
+
+/* ---------------------------------------------------------------- Q-prep --
+ * Replaces launch_q_absorbed (mla_kernels.cu:599-767): steps 2a1 (x @ W_q_a),
+ * 2a-norm (RMSNorm with gain), 2a2 (@ W_q_b), 2b (RoPE, theta 10000,
+ * interleaved pairs) and 2c (q_nope @ W_uk[h]).
+ *
+ *   x          [batch, sq, hidden]                 storage dtype
+ *   W_q_a      [hidden, q_lora]
+ *   q_norm_w   [q_lora]
+ *   W_q_b      [q_lora, heads*(nope+rope)]
+ *   W_uk       [heads, nope, kv_rank]
+ *   positions  [sq] int64 on the device, absolute position of each query
+ *   q_absorbed [batch, sq, heads, kv_rank]         output, storage dtype
+ *   q_rope     [batch, sq, heads, rope]            output, storage dtype
+ *
+ * `rope` must be even. The workspace must hold at least the number of bytes
+ * reported by mla_q_absorbed_workspace_size for the same arguments.
+ */
+MLA_API mla_status_t mla_q_absorbed_workspace_size(
+    mla_dtype_t dtype, mla_precision_t precision,
+    int64_t batch, int64_t sq, int64_t hidden, int64_t q_lora,
+    int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank,
+    size_t* bytes);
+
+MLA_API mla_status_t mla_q_absorbed(
+    mla_dtype_t dtype, mla_precision_t precision,
+    const void* x, const void* W_q_a, const void* q_norm_w,
+    const void* W_q_b, const void* W_uk, const int64_t* positions,
+    int64_t batch, int64_t sq, int64_t hidden, int64_t q_lora,
+    int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank,
+    double eps,
+    void* q_absorbed, void* q_rope,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------- attention --
+ * Replaces launch_mla_attention (mla_kernels.cu:1479-1682): scores
+ * (q_absorbed . c_kv + q_rope . pe_cache) / scale, softmax over the keys,
+ * ctx = P @ c_kv, out = ctx @ W_uv[h]^T.
+ *
+ *   q_absorbed [batch, sq, heads, kv_rank]
+ *   q_rope     [batch, sq, heads, rope]
+ *   c_kv       [batch, sk, kv_rank]
+ *   pe_cache   [batch, sk, rope]           shared by all heads
+ *   W_uv       [heads, v_dim, kv_rank]
+ *   out        [batch, sq, heads, v_dim]   output, storage dtype
+ *
+ * `scale` divides the scores (the reference passes sqrt(192), not its
+ * reciprocal: mla_kernels.cu:851). `causal` = 0 is the reference's semantics
+ * (every query attends all sk keys); 1 lets query i of sq attend keys
+ * 0 .. sk-sq+i only (requires sk >= sq). sk == 0 yields zeros.
+ */
+MLA_API mla_status_t mla_attention_workspace_size(
+    mla_dtype_t dtype, mla_precision_t precision,
+    int64_t batch, int64_t sq, int64_t sk, int64_t heads,
+    int64_t kv_rank, int64_t rope, int64_t v_dim, int causal,
+    size_t* bytes);
+
+MLA_API mla_status_t mla_attention(
+    mla_dtype_t dtype, mla_precision_t precision,
+    const void* q_absorbed, const void* q_rope,
+    const void* c_kv, const void* pe_cache, const void* W_uv,
+    int64_t batch, int64_t sq, int64_t sk, int64_t heads,
+    int64_t kv_rank, int64_t rope, int64_t v_dim,
+    double scale, int causal,
+    void* out,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MLA_B200_H_ */

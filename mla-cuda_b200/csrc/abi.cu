@@ -1,0 +1,200 @@
+// C-ABI entry points (include/mla_b200.h): argument validation, dtype and
+// precision dispatch, workspace sizing and error reporting. The validation
+// mirrors the reference's TORCH_CHECKs (mla_kernels.cu:627-635) and adds the
+// checks the reference's attention launcher leaves out (mla_kernels.cu:1487-1491
+// performs none).
+#include "qprep.cuh"
+#include "tc.cuh"
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+namespace mla {
+
+namespace {
+thread_local char g_last_error[512] = "";
+}
+
+mla_status_t set_error(mla_status_t st, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return st;
+}
+
+mla_status_t check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return set_error(MLA_ERR_CUDA, "MLA: launch of %s failed: %s", what, cudaGetErrorString(e));
+    return MLA_OK;
+}
+
+int sm_count() {
+    constexpr int kMaxDev = 64;
+    static int cached[kMaxDev] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+    if (cached[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+namespace {
+
+mla_status_t validate_q(mla_dtype_t dtype, mla_precision_t prec, int64_t batch, int64_t sq, int64_t hidden,
+                        int64_t q_lora, int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank) {
+    if (dtype < MLA_DTYPE_F32 || dtype > MLA_DTYPE_BF16)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: unknown dtype %d", int(dtype));
+    if (prec != MLA_PREC_EXACT && prec != MLA_PREC_TENSOR)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: unknown precision %d", int(prec));
+    if (batch < 0 || sq < 0 || hidden <= 0 || q_lora <= 0 || heads <= 0 || nope <= 0 || rope < 0 || kv_rank <= 0)
+        return set_error(MLA_ERR_INVALID_ARGUMENT,
+                         "MLA q_absorbed: sizes must be positive (batch=%lld sq=%lld hidden=%lld q_lora=%lld "
+                         "heads=%lld nope=%lld rope=%lld kv_rank=%lld)",
+                         (long long)batch, (long long)sq, (long long)hidden, (long long)q_lora, (long long)heads,
+                         (long long)nope, (long long)rope, (long long)kv_rank);
+    if (rope % 2 != 0 || rope / 2 > kMaxRopePairs)
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA q_absorbed: rope_dim must be even and <= %d (got %lld)",
+                         2 * kMaxRopePairs, (long long)rope);
+    return MLA_OK;
+}
+
+mla_status_t validate_a(mla_dtype_t dtype, mla_precision_t prec, int64_t batch, int64_t sq, int64_t sk,
+                        int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim, int causal) {
+    if (dtype < MLA_DTYPE_F32 || dtype > MLA_DTYPE_BF16)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: unknown dtype %d", int(dtype));
+    if (prec != MLA_PREC_EXACT && prec != MLA_PREC_TENSOR)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: unknown precision %d", int(prec));
+    if (batch < 0 || sq < 0 || sk < 0 || heads <= 0 || kv_rank <= 0 || rope < 0 || v_dim <= 0)
+        return set_error(MLA_ERR_INVALID_ARGUMENT,
+                         "MLA mla_attention: invalid sizes (batch=%lld sq=%lld sk=%lld heads=%lld kv_rank=%lld "
+                         "rope=%lld v_dim=%lld)",
+                         (long long)batch, (long long)sq, (long long)sk, (long long)heads, (long long)kv_rank,
+                         (long long)rope, (long long)v_dim);
+    if (causal && sk < sq)
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: causal masking needs sk >= sq (sk=%lld sq=%lld)",
+                         (long long)sk, (long long)sq);
+    if (batch > 65535)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA mla_attention: batch > 65535 is not supported (got %lld)",
+                         (long long)batch);
+    return MLA_OK;
+}
+
+template <typename F>
+auto dispatch(mla_dtype_t dt, F&& f) {
+    switch (dt) {
+        case MLA_DTYPE_F64: return f(double{});
+        case MLA_DTYPE_F16: return f(__half{});
+        case MLA_DTYPE_BF16: return f(__nv_bfloat16{});
+        default: return f(float{});
+    }
+}
+
+bool use_tc_attention(mla_dtype_t dt, mla_precision_t prec, const AArgs& a) {
+    return prec == MLA_PREC_TENSOR && dt != MLA_DTYPE_F64 && tc_attention_supported(a);
+}
+
+}  // namespace
+}  // namespace mla
+
+using namespace mla;
+
+extern "C" {
+
+int mla_abi_version(void) { return MLA_B200_ABI_VERSION; }
+
+const char* mla_status_string(mla_status_t s) {
+    switch (s) {
+        case MLA_OK: return "ok";
+        case MLA_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case MLA_ERR_UNSUPPORTED: return "unsupported";
+        case MLA_ERR_WORKSPACE: return "workspace too small";
+        case MLA_ERR_CUDA: return "CUDA error";
+    }
+    return "unknown status";
+}
+
+const char* mla_last_error_message(void) { return g_last_error; }
+
+mla_status_t mla_q_absorbed_workspace_size(mla_dtype_t dtype, mla_precision_t precision, int64_t batch, int64_t sq,
+                                           int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope, int64_t rope,
+                                           int64_t kv_rank, size_t* bytes) {
+    MLA_TRY(validate_q(dtype, precision, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank));
+    if (!bytes) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA: bytes must not be NULL");
+    QArgs a{};
+    a.batch = batch; a.sq = sq; a.hidden = hidden; a.q_lora = q_lora;
+    a.heads = heads; a.nope = nope; a.rope = rope; a.kv_rank = kv_rank;
+    *bytes = dispatch(dtype, [&](auto t) { return qprep_exact_workspace<decltype(t)>(a); });
+    return MLA_OK;
+}
+
+mla_status_t mla_q_absorbed(mla_dtype_t dtype, mla_precision_t precision, const void* x, const void* W_q_a,
+                            const void* q_norm_w, const void* W_q_b, const void* W_uk, const int64_t* positions,
+                            int64_t batch, int64_t sq, int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope,
+                            int64_t rope, int64_t kv_rank, double eps, void* q_absorbed, void* q_rope,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+    MLA_TRY(validate_q(dtype, precision, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank));
+    if (batch * sq == 0) return MLA_OK;
+    if (!x || !W_q_a || !q_norm_w || !W_q_b || !W_uk || !positions || !q_absorbed || (rope > 0 && !q_rope))
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA q_absorbed: null operand pointer");
+    QArgs a{x, W_q_a, q_norm_w, W_q_b, W_uk, positions, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank,
+            eps, q_absorbed, q_rope, workspace, workspace_bytes};
+    const size_t need = dispatch(dtype, [&](auto t) { return qprep_exact_workspace<decltype(t)>(a); });
+    if (need > 0 && (!workspace || workspace_bytes < need))
+        return set_error(MLA_ERR_WORKSPACE, "MLA q_absorbed: workspace of %zu bytes needed, %zu given", need,
+                         workspace ? workspace_bytes : size_t(0));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto t) { return qprep_exact<decltype(t)>(a, st); });
+}
+
+mla_status_t mla_attention_workspace_size(mla_dtype_t dtype, mla_precision_t precision, int64_t batch, int64_t sq,
+                                          int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim,
+                                          int causal, size_t* bytes) {
+    MLA_TRY(validate_a(dtype, precision, batch, sq, sk, heads, kv_rank, rope, v_dim, causal));
+    if (!bytes) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA: bytes must not be NULL");
+    AArgs a{};
+    a.batch = batch; a.sq = sq; a.sk = sk; a.heads = heads; a.kv_rank = kv_rank; a.rope = rope; a.v_dim = v_dim;
+    a.causal = causal;
+    if (use_tc_attention(dtype, precision, a))
+        *bytes = dispatch(dtype, [&](auto t) { return tc_attention_workspace<decltype(t)>(a); });
+    else
+        *bytes = dispatch(dtype, [&](auto t) { return attn_exact_workspace<decltype(t)>(a); });
+    return MLA_OK;
+}
+
+mla_status_t mla_attention(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed, const void* q_rope,
+                           const void* c_kv, const void* pe_cache, const void* W_uv, int64_t batch, int64_t sq,
+                           int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim, double scale,
+                           int causal, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    MLA_TRY(validate_a(dtype, precision, batch, sq, sk, heads, kv_rank, rope, v_dim, causal));
+    if (batch * sq == 0) return MLA_OK;
+    if (!out || !W_uv || !q_absorbed) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: null pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (sk == 0) {
+        // Softmax over no keys: the reference's einsums reduce over an empty axis.
+        const size_t esz = dtype == MLA_DTYPE_F64 ? 8 : dtype == MLA_DTYPE_F32 ? 4 : 2;
+        if (cudaMemsetAsync(out, 0, size_t(batch * sq * heads * v_dim) * esz, st) != cudaSuccess)
+            return set_error(MLA_ERR_CUDA, "MLA mla_attention: memset failed");
+        return MLA_OK;
+    }
+    if (!c_kv || (rope > 0 && (!q_rope || !pe_cache)))
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: null operand pointer");
+    if (scale == 0.0) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: scale must be non-zero");
+    AArgs a{q_absorbed, q_rope, c_kv, pe_cache, W_uv, batch, sq, sk, heads, kv_rank, rope, v_dim,
+            scale, causal, out, workspace, workspace_bytes};
+    const bool tc = use_tc_attention(dtype, precision, a);
+    const size_t need = tc ? dispatch(dtype, [&](auto t) { return tc_attention_workspace<decltype(t)>(a); })
+                           : dispatch(dtype, [&](auto t) { return attn_exact_workspace<decltype(t)>(a); });
+    if (need > 0 && (!workspace || workspace_bytes < need))
+        return set_error(MLA_ERR_WORKSPACE, "MLA mla_attention: workspace of %zu bytes needed, %zu given", need,
+                         workspace ? workspace_bytes : size_t(0));
+    if (tc) return dispatch(dtype, [&](auto t) { return tc_attention<decltype(t)>(a, st); });
+    return dispatch(dtype, [&](auto t) { return attn_exact<decltype(t)>(a, st); });
+}
+
+}  // extern "C"

@@ -1,0 +1,54 @@
+// Shared definitions for the MLA B200 kernels: dtype traits, status plumbing,
+// small math helpers. Everything here is header-only and device/host neutral.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "mla_b200.h"
+
+namespace mla {
+
+// Accumulate dtype policy: fp64 storage accumulates in fp64, every other
+// storage dtype in fp32. Same policy as the reference's AccType
+// (mla_kernels.cu:118-120), extended to bf16.
+template <typename T> struct AccOf { using type = float; };
+template <> struct AccOf<double> { using type = double; };
+template <typename T> using acc_t = typename AccOf<T>::type;
+
+template <typename To, typename From>
+__device__ __forceinline__ To cvt(From v) { return static_cast<To>(v); }
+template <> __device__ __forceinline__ float cvt<float, __half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float cvt<float, __nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ __half cvt<__half, float>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16, float>(float v) { return __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float fexp(float x) { return expf(x); }
+__device__ __forceinline__ double fexp(double x) { return exp(x); }
+
+template <typename A> __device__ __forceinline__ A neg_inf();
+template <> __device__ __forceinline__ float neg_inf<float>() { return -__int_as_float(0x7f800000); }
+template <> __device__ __forceinline__ double neg_inf<double>() { return -__longlong_as_double(0x7ff0000000000000LL); }
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Records a message for mla_last_error_message() and returns the status.
+mla_status_t set_error(mla_status_t st, const char* fmt, ...);
+
+// Checks the launch that just happened on this thread.
+mla_status_t check_launch(const char* what);
+
+// Number of SMs of the current device, cached per device.
+int sm_count();
+
+}  // namespace mla
+
+#define MLA_TRY(expr)                                  \
+    do {                                               \
+        mla_status_t _st = (expr);                     \
+        if (_st != MLA_OK) return _st;                 \
+    } while (0)

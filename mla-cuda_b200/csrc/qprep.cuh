@@ -1,0 +1,35 @@
+// Argument bundles and entry points of the Q-prep and attention stages, shared
+// by the C-ABI layer (abi.cu) and the kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace mla {
+
+constexpr int kMaxRopePairs = 128;   // rope <= 256
+
+struct QArgs {
+    const void* x; const void* W_q_a; const void* q_norm_w; const void* W_q_b; const void* W_uk;
+    const int64_t* positions;
+    int64_t batch, sq, hidden, q_lora, heads, nope, rope, kv_rank;
+    double eps;
+    void* q_absorbed; void* q_rope;
+    void* workspace; size_t workspace_bytes;
+};
+
+struct AArgs {
+    const void* q_absorbed; const void* q_rope; const void* c_kv; const void* pe_cache; const void* W_uv;
+    int64_t batch, sq, sk, heads, kv_rank, rope, v_dim;
+    double scale;
+    int causal;
+    void* out;
+    void* workspace; size_t workspace_bytes;
+};
+
+template <typename T> size_t qprep_exact_workspace(const QArgs& a);
+template <typename T> mla_status_t qprep_exact(const QArgs& a, cudaStream_t st);
+
+template <typename T> size_t attn_exact_workspace(const AArgs& a);
+template <typename T> mla_status_t attn_exact(const AArgs& a, cudaStream_t st);
+
+}  // namespace mla

@@ -1,0 +1,326 @@
+// Q-prep in exact arithmetic (MLA_PREC_EXACT): steps 2a1, 2a-norm, 2a2, 2b and
+// 2c of the absorbed MLA forward on CUDA cores, for fp32 / fp64 / fp16 / bf16
+// storage. Reference semantics: launch_q_absorbed (mla_kernels.cu:599-767) and
+// the PyTorch path prepare_q_mla_absorbed (exhaustive_benchmark_suite.py:268-286).
+//
+//   2a1  P1[z] = x[:, kz] @ W_q_a[kz, :]            split-K partials (acc dtype)
+//   2an  q_lat = T( sum_z P1[z] * rsqrt(mean(.^2)+eps) * gain )
+//   2a2  P2[z] = q_lat[:, kz] @ W_q_b[kz, :]        split-K partials (acc dtype)
+//   2b   q_nope = sum_z P2[z][.., nope cols], q_rope = T(RoPE(sum_z P2[z][.., rope cols]))
+//   2c   q_absorbed[:, h] = T(q_nope[:, h] @ W_uk[h])
+//
+// Split-K partials are reduced by the next kernel, never with atomics, so the
+// result is deterministic run to run.
+#include "qprep.cuh"
+#include "simt_gemm.cuh"
+
+#include <cmath>
+
+namespace mla {
+namespace {
+
+// C[z][m][n] = sum_{k in slice z} A[m][k] * B[k][n]; A and B row-major.
+template <typename TA, typename TB, typename Acc>
+struct ProjProblem {
+    static constexpr bool kAKFast = true;
+    static constexpr bool kBNFast = true;
+    const TA* A; const TB* B;
+    int64_t lda, ldb, M, N, m0, n0;
+    __device__ Acc a(int64_t ml, int64_t k) const {
+        const int64_t m = m0 + ml;
+        return (m < M) ? cvt<Acc>(A[m * lda + k]) : Acc(0);
+    }
+    __device__ Acc b(int64_t k, int64_t nl) const {
+        const int64_t n = n0 + nl;
+        return (n < N) ? cvt<Acc>(B[k * ldb + n]) : Acc(0);
+    }
+};
+
+// One launch of a split-K projection. grid = (n tiles, m tiles, splits).
+template <class Cfg, typename TA, typename TB>
+__global__ void __launch_bounds__(256) proj_splitk_kernel(
+    const TA* __restrict__ A, const TB* __restrict__ B, typename Cfg::Acc* __restrict__ C,
+    int64_t M, int64_t N, int64_t K, int64_t k_chunk)
+{
+    using Acc = typename Cfg::Acc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    ProjProblem<TA, TB, Acc> p{A, B, K, N, M, N,
+                               int64_t(blockIdx.y) * Cfg::BM, int64_t(blockIdx.x) * Cfg::BN};
+    const int64_t kb = int64_t(blockIdx.z) * k_chunk;
+    const int64_t ke = (kb + k_chunk < K) ? kb + k_chunk : K;
+    Acc acc[Cfg::TM][Cfg::TN];
+    simt_gemm_mainloop<Cfg>(p, kb, ke, acc, reinterpret_cast<Acc*>(smem_raw));
+    const int tx = threadIdx.x % Cfg::kTX, ty = threadIdx.x / Cfg::kTX;
+    Acc* Cz = C + int64_t(blockIdx.z) * M * N;
+#pragma unroll
+    for (int i = 0; i < Cfg::TM; ++i) {
+        const int64_t m = p.m0 + Cfg::m_of(ty, i);
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < Cfg::TN; ++j) {
+            const int64_t n = p.n0 + Cfg::n_of(tx, j);
+            if (n < N) Cz[m * N + n] = acc[i][j];
+        }
+    }
+}
+
+// 2a-norm: one block per row. Sums the split-K partials, RMS-normalises with
+// the gain and narrows to the storage dtype (the reference hands the latent to
+// 2a2 in the input dtype: mla_kernels.cu:416-419).
+template <typename T>
+__global__ void __launch_bounds__(256) lat_norm_kernel(
+    const acc_t<T>* __restrict__ P1, int splits, const T* __restrict__ gain,
+    T* __restrict__ q_lat, int64_t M, int64_t q_lora, acc_t<T> eps)
+{
+    using Acc = acc_t<T>;
+    const int64_t m = blockIdx.x;
+    auto val = [&](int64_t n) {
+        Acc v = Acc(0);
+        for (int z = 0; z < splits; ++z) v += P1[(int64_t(z) * M + m) * q_lora + n];
+        return v;
+    };
+    Acc ss = Acc(0);
+    for (int64_t n = threadIdx.x; n < q_lora; n += blockDim.x) {
+        const Acc v = val(n);
+        ss = fma(v, v, ss);
+    }
+    __shared__ Acc red[32];
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        Acc t = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : Acc(0);
+        for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+        if (threadIdx.x == 0) red[0] = Acc(1) / sqrt(t / Acc(q_lora) + eps);
+    }
+    __syncthreads();
+    const Acc inv_rms = red[0];
+    for (int64_t n = threadIdx.x; n < q_lora; n += blockDim.x)
+        q_lat[m * q_lora + n] = cvt<T>(val(n) * inv_rms * cvt<Acc>(gain[n]));
+}
+
+// 2b: reduce the 2a2 partials of every head into q_nope (acc dtype, the left
+// operand of 2c) and rotate the rope slice. Interleaved pairs (2j, 2j+1) are
+// rotated by pos * inv_freq[j], inv_freq[j] = 1 / 10000^(2j/rope), the
+// convention of apply_rope (exhaustive_benchmark_suite.py:210-232).
+template <typename T>
+struct RopeTable { acc_t<T> inv_freq[kMaxRopePairs]; };
+
+template <typename T>
+__global__ void __launch_bounds__(256) rope_gather_kernel(
+    const acc_t<T>* __restrict__ P2, int splits, const int64_t* __restrict__ positions,
+    acc_t<T>* __restrict__ q_nope, T* __restrict__ q_rope,
+    int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, RopeTable<T> tab)
+{
+    using Acc = acc_t<T>;
+    const int64_t qk = nope + rope;
+    const int64_t ncols = heads * qk;
+    const int64_t per_head = nope + rope / 2;
+    const int64_t total = M * heads * per_head;
+    for (int64_t idx = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; idx < total;
+         idx += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t e = idx % per_head;
+        const int64_t mh = idx / per_head;
+        const int64_t h = mh % heads;
+        const int64_t m = mh / heads;
+        const int64_t col = h * qk + (e < nope ? e : nope + 2 * (e - nope));
+        auto sum = [&](int64_t c) {
+            Acc v = Acc(0);
+            for (int z = 0; z < splits; ++z) v += P2[(int64_t(z) * M + m) * ncols + c];
+            return v;
+        };
+        if (e < nope) {
+            q_nope[mh * nope + e] = sum(col);
+        } else {
+            const int64_t j = e - nope;
+            const Acc ev = sum(col), od = sum(col + 1);
+            const Acc ang = Acc(positions[m % sq]) * tab.inv_freq[j];
+            // cos/sin are narrowed to the storage dtype before use, as apply_rope does
+            // (exhaustive_benchmark_suite.py:222-223); a no-op for fp32/fp64.
+            const Acc c = cvt<Acc>(cvt<T>(cos(ang)));
+            const Acc s = cvt<Acc>(cvt<T>(sin(ang)));
+            q_rope[mh * rope + 2 * j] = cvt<T>(ev * c - od * s);
+            q_rope[mh * rope + 2 * j + 1] = cvt<T>(ev * s + od * c);
+        }
+    }
+}
+
+// 2c: q_absorbed[m, h, :] = q_nope[m, h, :] @ W_uk[h]. grid = (n tiles, m tiles, heads).
+template <typename T, typename Acc>
+struct AbsorbProblem {
+    static constexpr bool kAKFast = true;
+    static constexpr bool kBNFast = true;
+    const Acc* qn; const T* W;
+    int64_t M, heads, nope, R, h, m0, n0;
+    __device__ Acc a(int64_t ml, int64_t k) const {
+        const int64_t m = m0 + ml;
+        return (m < M) ? qn[(m * heads + h) * nope + k] : Acc(0);
+    }
+    __device__ Acc b(int64_t k, int64_t nl) const {
+        const int64_t n = n0 + nl;
+        return (n < R) ? cvt<Acc>(W[(h * nope + k) * R + n]) : Acc(0);
+    }
+};
+
+template <class Cfg, typename T>
+__global__ void __launch_bounds__(256) absorb_kernel(
+    const typename Cfg::Acc* __restrict__ q_nope, const T* __restrict__ W_uk,
+    T* __restrict__ q_abs, int64_t M, int64_t heads, int64_t nope, int64_t R)
+{
+    using Acc = typename Cfg::Acc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    AbsorbProblem<T, Acc> p{q_nope, W_uk, M, heads, nope, R, int64_t(blockIdx.z),
+                            int64_t(blockIdx.y) * Cfg::BM, int64_t(blockIdx.x) * Cfg::BN};
+    Acc acc[Cfg::TM][Cfg::TN];
+    simt_gemm_mainloop<Cfg>(p, 0, nope, acc, reinterpret_cast<Acc*>(smem_raw));
+    const int tx = threadIdx.x % Cfg::kTX, ty = threadIdx.x / Cfg::kTX;
+#pragma unroll
+    for (int i = 0; i < Cfg::TM; ++i) {
+        const int64_t m = p.m0 + Cfg::m_of(ty, i);
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < Cfg::TN; ++j) {
+            const int64_t n = p.n0 + Cfg::n_of(tx, j);
+            if (n < R) q_abs[(m * heads + p.h) * R + n] = cvt<T>(acc[i][j]);
+        }
+    }
+}
+
+struct QPlan {
+    bool small;          // 16-row tiles (B*Sq <= 16)
+    int64_t bm, bn, bk;
+    int split1, split2;
+    int64_t chunk1, chunk2;
+    size_t off_p1, off_qlat, off_p2, off_qnope, total;
+};
+
+// Split-K plan: enough CTAs for ~4 resident waves, each split a whole number of
+// K tiles, no empty split.
+void plan_split(int64_t tiles, int64_t K, int64_t bk, int& split, int64_t& chunk) {
+    const int64_t want = 4LL * 2 * sm_count();
+    int64_t s = want / (tiles > 0 ? tiles : 1);
+    const int64_t ktiles = ceil_div(K, bk);
+    if (s > ktiles / 2) s = ktiles / 2;    // keep at least two K tiles per split
+    if (s < 1) s = 1;
+    const int64_t chunk_tiles = ceil_div(ktiles, s);
+    s = ceil_div(ktiles, chunk_tiles);
+    split = int(s);
+    chunk = chunk_tiles * bk;
+}
+
+template <typename T>
+QPlan make_plan(const QArgs& a) {
+    using Acc = acc_t<T>;
+    QPlan p{};
+    const int64_t M = a.batch * a.sq;
+    p.small = M <= 16;
+    p.bm = p.small ? CfgSmall<Acc>::BM : CfgBig<Acc>::BM;
+    p.bn = p.small ? CfgSmall<Acc>::BN : CfgBig<Acc>::BN;
+    p.bk = p.small ? CfgSmall<Acc>::BK : CfgBig<Acc>::BK;
+    const int64_t mt = ceil_div(M, p.bm);
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    plan_split(mt * ceil_div(a.q_lora, p.bn), a.hidden, p.bk, p.split1, p.chunk1);
+    plan_split(mt * ceil_div(ncols, p.bn), a.q_lora, p.bk, p.split2, p.chunk2);
+    size_t off = 0;
+    p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(Acc), 256);
+    p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(T), 256);
+    p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(Acc), 256);
+    p.off_qnope = off; off = align_up(off + size_t(M) * a.heads * a.nope * sizeof(Acc), 256);
+    p.total = off;
+    return p;
+}
+
+template <class Cfg, typename TA, typename TB>
+mla_status_t launch_proj(const TA* A, const TB* B, typename Cfg::Acc* C, int64_t M, int64_t N,
+                         int64_t K, int split, int64_t chunk, cudaStream_t st) {
+    auto kern = proj_splitk_kernel<Cfg, TA, TB>;
+    if (Cfg::kSmemBytes > 48 * 1024)
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmemBytes));
+    dim3 grid(unsigned(ceil_div(N, Cfg::BN)), unsigned(ceil_div(M, Cfg::BM)), unsigned(split));
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(A, B, C, M, N, K, chunk);
+    return check_launch("q projection");
+}
+
+template <class Cfg, typename T>
+mla_status_t launch_absorb(const typename Cfg::Acc* qn, const T* W, T* out, const QArgs& a,
+                           int64_t M, cudaStream_t st) {
+    auto kern = absorb_kernel<Cfg, T>;
+    if (Cfg::kSmemBytes > 48 * 1024)
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(Cfg::kSmemBytes));
+    dim3 grid(unsigned(ceil_div(a.kv_rank, Cfg::BN)), unsigned(ceil_div(M, Cfg::BM)), unsigned(a.heads));
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(qn, W, out, M, a.heads, a.nope, a.kv_rank);
+    return check_launch("q absorb (2c)");
+}
+
+}  // namespace
+
+template <typename T>
+size_t qprep_exact_workspace(const QArgs& a) { return make_plan<T>(a).total; }
+
+template <typename T>
+mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
+    using Acc = acc_t<T>;
+    const QPlan p = make_plan<T>(a);
+    const int64_t M = a.batch * a.sq;
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    char* ws = static_cast<char*>(a.workspace);
+    Acc* P1 = reinterpret_cast<Acc*>(ws + p.off_p1);
+    T* q_lat = reinterpret_cast<T*>(ws + p.off_qlat);
+    Acc* P2 = reinterpret_cast<Acc*>(ws + p.off_p2);
+    Acc* q_nope = reinterpret_cast<Acc*>(ws + p.off_qnope);
+    const T* x = static_cast<const T*>(a.x);
+    const T* Wqa = static_cast<const T*>(a.W_q_a);
+    const T* Wqb = static_cast<const T*>(a.W_q_b);
+
+    if (p.small) {
+        MLA_TRY((launch_proj<CfgSmall<Acc>, T, T>(x, Wqa, P1, M, a.q_lora, a.hidden, p.split1, p.chunk1, st)));
+    } else {
+        MLA_TRY((launch_proj<CfgBig<Acc>, T, T>(x, Wqa, P1, M, a.q_lora, a.hidden, p.split1, p.chunk1, st)));
+    }
+    lat_norm_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, p.split1, static_cast<const T*>(a.q_norm_w),
+                                                     q_lat, M, a.q_lora, Acc(a.eps));
+    MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
+    if (p.small) {
+        MLA_TRY((launch_proj<CfgSmall<Acc>, T, T>(q_lat, Wqb, P2, M, ncols, a.q_lora, p.split2, p.chunk2, st)));
+    } else {
+        MLA_TRY((launch_proj<CfgBig<Acc>, T, T>(q_lat, Wqb, P2, M, ncols, a.q_lora, p.split2, p.chunk2, st)));
+    }
+
+    RopeTable<T> tab{};
+    for (int64_t j = 0; j < a.rope / 2; ++j) {
+        // Rounded the way torch computes 1 / 10000 ** (2j / rope) in the
+        // accumulate dtype: a correctly rounded power, then an IEEE divide.
+        const double pw = std::pow(10000.0, double(2 * j) / double(a.rope));
+        tab.inv_freq[j] = Acc(1) / Acc(pw);
+    }
+    {
+        const int64_t total = M * a.heads * (a.nope + a.rope / 2);
+        int64_t blocks = ceil_div(total, 256);
+        const int64_t cap = 16LL * sm_count();
+        if (blocks > cap) blocks = cap;
+        if (blocks < 1) blocks = 1;
+        rope_gather_kernel<T><<<unsigned(blocks), 256, 0, st>>>(
+            P2, p.split2, a.positions, q_nope, static_cast<T*>(a.q_rope),
+            M, a.sq, a.heads, a.nope, a.rope, tab);
+        MLA_TRY(check_launch("q rope (2b)"));
+    }
+    if (p.small) {
+        MLA_TRY((launch_absorb<CfgSmall<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk),
+                                                 static_cast<T*>(a.q_absorbed), a, M, st)));
+    } else {
+        MLA_TRY((launch_absorb<CfgBig<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk),
+                                               static_cast<T*>(a.q_absorbed), a, M, st)));
+    }
+    return MLA_OK;
+}
+
+template size_t qprep_exact_workspace<float>(const QArgs&);
+template size_t qprep_exact_workspace<double>(const QArgs&);
+template size_t qprep_exact_workspace<__half>(const QArgs&);
+template size_t qprep_exact_workspace<__nv_bfloat16>(const QArgs&);
+template mla_status_t qprep_exact<float>(const QArgs&, cudaStream_t);
+template mla_status_t qprep_exact<double>(const QArgs&, cudaStream_t);
+template mla_status_t qprep_exact<__half>(const QArgs&, cudaStream_t);
+template mla_status_t qprep_exact<__nv_bfloat16>(const QArgs&, cudaStream_t);
+
+}  // namespace mla

@@ -1,0 +1,14 @@
+// Tensor-core (tcgen05) attention path, MLA_PREC_TENSOR.
+#pragma once
+
+#include "qprep.cuh"
+
+namespace mla {
+
+// True when the tensor-core kernel covers this shape (otherwise the exact
+// path runs).
+bool tc_attention_supported(const AArgs& a);
+template <typename T> size_t tc_attention_workspace(const AArgs& a);
+template <typename T> mla_status_t tc_attention(const AArgs& a, cudaStream_t st);
+
+}  // namespace mla

@@ -1,0 +1,234 @@
+"""Drop-in replacement of the reference's ``mla_custom_cuda`` extension module.
+
+The reference builds ``mla_custom_cuda`` from ``mla_kernels.cu`` with pybind11
+and exposes two functions (mla_kernels.cu:1688-1692):
+
+    q_absorbed(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim, rope_dim, eps)
+        -> [q_absorbed, q_rope]
+    mla_attention(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale) -> out
+
+This module keeps those names, positional signatures, return types and error
+behaviour (shape errors raise ``RuntimeError``, like TORCH_CHECK) and runs the
+B200 kernels of ``libmla_b200.so`` through its C ABI (include/mla_b200.h).
+Outputs and workspaces are allocated with torch's caching allocator on the
+inputs' device, and all work is enqueued on torch's current stream, as in the
+reference (mla_kernels.cu:664-667, :1528-1549).
+
+There is no CPU or PyTorch fallback: importing this module fails if the
+library is missing, and every call requires CUDA tensors.
+
+Precision: the default, ``"exact"``, computes in the accumulate dtype like the
+reference (fp64 for fp64 tensors, fp32 otherwise). ``"tensor"`` runs the
+tcgen05 tensor-core kernels (bf16 operands, fp32 accumulation) where they cover
+the shape. Select it with ``set_precision("tensor")``, the ``MLA_PRECISION``
+environment variable, or the ``precision=`` argument of the ``*_ex`` calls.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from pathlib import Path
+from typing import List, Optional
+
+import torch
+
+__all__ = [
+    "q_absorbed", "mla_attention", "q_absorbed_ex", "mla_attention_ex",
+    "set_precision", "get_precision", "library_path", "abi_version",
+]
+
+_LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmla_b200.so"
+
+_DTYPE_CODES = {torch.float32: 0, torch.float64: 1, torch.float16: 2, torch.bfloat16: 3}
+_PRECISIONS = {"exact": 0, "tensor": 1}
+
+_c_i64 = ctypes.c_int64
+_c_vp = ctypes.c_void_p
+_c_size = ctypes.c_size_t
+
+
+def _load() -> ctypes.CDLL:
+    if not _LIB_PATH.exists():
+        raise ImportError(
+            f"mla_custom_cuda: {_LIB_PATH} is missing; build it with "
+            f"`python mla-cuda_b200/build.py` (there is no CPU fallback)")
+    lib = ctypes.CDLL(str(_LIB_PATH))
+    lib.mla_abi_version.restype = ctypes.c_int
+    lib.mla_status_string.restype = ctypes.c_char_p
+    lib.mla_status_string.argtypes = [ctypes.c_int]
+    lib.mla_last_error_message.restype = ctypes.c_char_p
+    lib.mla_q_absorbed_workspace_size.restype = ctypes.c_int
+    lib.mla_q_absorbed_workspace_size.argtypes = [ctypes.c_int, ctypes.c_int] + [_c_i64] * 8 + [
+        ctypes.POINTER(_c_size)]
+    lib.mla_q_absorbed.restype = ctypes.c_int
+    lib.mla_q_absorbed.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_vp] * 6 + [_c_i64] * 8
+                                   + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
+    lib.mla_attention_workspace_size.restype = ctypes.c_int
+    lib.mla_attention_workspace_size.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_i64] * 7
+                                                 + [ctypes.c_int, ctypes.POINTER(_c_size)])
+    lib.mla_attention.restype = ctypes.c_int
+    lib.mla_attention.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_vp] * 5 + [_c_i64] * 7
+                                  + [ctypes.c_double, ctypes.c_int, _c_vp, _c_vp, _c_size, _c_vp])
+    return lib
+
+
+_lib = _load()
+_precision = os.environ.get("MLA_PRECISION", "exact").strip().lower()
+if _precision not in _PRECISIONS:
+    raise ImportError(f"mla_custom_cuda: MLA_PRECISION must be one of {sorted(_PRECISIONS)}")
+
+
+def library_path() -> str:
+    """Path of the loaded C-ABI library."""
+    return str(_LIB_PATH)
+
+
+def abi_version() -> int:
+    return int(_lib.mla_abi_version())
+
+
+def set_precision(precision: str) -> None:
+    """Default arithmetic of later calls: "exact" or "tensor"."""
+    global _precision
+    p = precision.strip().lower()
+    if p not in _PRECISIONS:
+        raise ValueError(f"precision must be one of {sorted(_PRECISIONS)}, got {precision!r}")
+    _precision = p
+
+
+def get_precision() -> str:
+    return _precision
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _raise_status(st: int, what: str) -> None:
+    if st != 0:
+        detail = _lib.mla_last_error_message().decode(errors="replace")
+        name = _lib.mla_status_string(st).decode(errors="replace")
+        raise RuntimeError(f"{what}: {name}: {detail}")
+
+
+def _prec_code(precision: Optional[str]) -> int:
+    p = _precision if precision is None else precision.strip().lower()
+    if p not in _PRECISIONS:
+        raise ValueError(f"precision must be one of {sorted(_PRECISIONS)}, got {precision!r}")
+    return _PRECISIONS[p]
+
+
+def _float_operands(name_tensors, device=None):
+    dtype = None
+    for name, t in name_tensors:
+        _check(isinstance(t, torch.Tensor), f"{name} must be a tensor")
+        _check(t.is_cuda, f"{name} must be a CUDA tensor (there is no CPU path)")
+        _check(t.dtype in _DTYPE_CODES, f"{name}: unsupported dtype {t.dtype}")
+        if dtype is None:
+            dtype, device = t.dtype, t.device
+        _check(t.dtype == dtype, f"{name} has dtype {t.dtype}, expected {dtype}")
+        _check(t.device == device, f"{name} is on {t.device}, expected {device}")
+    return dtype, device
+
+
+def q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim: int, rope_dim: int,
+                  eps: float, precision: Optional[str] = None) -> List[torch.Tensor]:
+    """q_absorbed with an explicit precision; see q_absorbed."""
+    dtype, device = _float_operands(
+        [("x", x), ("W_q_a", W_q_a), ("q_norm_w", q_norm_w), ("W_q_b", W_q_b), ("W_uk", W_uk)])
+    _check(x.dim() == 3, f"x must be [B, Sq, hidden] (got {tuple(x.shape)})")
+    _check(W_q_a.dim() == 2, f"W_q_a must be [hidden, q_lora] (got {tuple(W_q_a.shape)})")
+    _check(W_uk.dim() == 3, f"W_uk must be [H, nope, kv_rank] (got {tuple(W_uk.shape)})")
+    B, Sq, hidden = x.shape
+    q_lora = W_q_a.shape[1]
+    H, nope_w, R = W_uk.shape
+    nope_dim, rope_dim = int(nope_dim), int(rope_dim)
+    qk = nope_dim + rope_dim
+    _check(W_q_a.shape[0] == hidden, "W_q_a must be [hidden, q_lora]")
+    _check(W_q_b.dim() == 2 and W_q_b.shape[0] == q_lora and W_q_b.shape[1] == H * qk,
+           "W_q_b must be [q_lora, H*(nope+rope)]")
+    _check(q_norm_w.dim() == 1 and q_norm_w.shape[0] == q_lora,
+           f"q_norm_w must be a 1-D tensor of length q_lora (got {list(q_norm_w.shape)})")
+    _check(nope_w == nope_dim, f"W_uk must be [H, nope_dim={nope_dim}, kv_rank] (got {tuple(W_uk.shape)})")
+    _check(isinstance(positions, torch.Tensor) and positions.dim() == 1 and positions.shape[0] == Sq,
+           f"positions must be a 1-D tensor of length Sq (got "
+           f"{list(positions.shape) if isinstance(positions, torch.Tensor) else type(positions)})")
+    _check(not positions.is_floating_point() and not positions.is_complex(),
+           "positions must be an integer tensor")
+    xc, Wa, g, Wb, Wk = (t.contiguous() for t in (x, W_q_a, q_norm_w, W_q_b, W_uk))
+    pos = positions.to(device=device, dtype=torch.int64).contiguous()
+    qa = torch.empty((B, Sq, H, R), dtype=dtype, device=device)
+    qr = torch.empty((B, Sq, H, rope_dim), dtype=dtype, device=device)
+    dt, pc = _DTYPE_CODES[dtype], _prec_code(precision)
+    nbytes = _c_size(0)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_q_absorbed_workspace_size(dt, pc, B, Sq, hidden, q_lora, H, nope_dim,
+                                                         rope_dim, R, ctypes.byref(nbytes)),
+                      "q_absorbed")
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        st = _lib.mla_q_absorbed(dt, pc, xc.data_ptr(), Wa.data_ptr(), g.data_ptr(), Wb.data_ptr(),
+                                 Wk.data_ptr(), pos.data_ptr(), B, Sq, hidden, q_lora, H, nope_dim,
+                                 rope_dim, R, float(eps), qa.data_ptr(), qr.data_ptr(), ws.data_ptr(),
+                                 ws.numel(), stream)
+    _raise_status(st, "q_absorbed")
+    return [qa, qr]
+
+
+def q_absorbed(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim: int, rope_dim: int,
+               eps: float) -> List[torch.Tensor]:
+    """Kernel 2 — Q path: wq_b(RMSNorm(x @ W_q_a)) -> absorb @ W_uk, RoPE on q_rope.
+
+    Same contract as the reference (mla_kernels.cu:599-767): returns
+    [q_absorbed [B,Sq,H,kv_rank], q_rope [B,Sq,H,rope_dim]] in the input dtype.
+    """
+    return q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim, rope_dim, eps)
+
+
+def mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float, causal: bool = False,
+                     precision: Optional[str] = None) -> torch.Tensor:
+    """mla_attention with an explicit precision and an optional causal mask.
+
+    causal=True lets query i of Sq attend keys 0 .. Sk-Sq+i (multi-token
+    decode); False is the reference's behaviour (all keys).
+    """
+    dtype, device = _float_operands([("q_absorbed", q_absorbed), ("q_rope", q_rope), ("c_kv", c_kv),
+                                     ("pe_cache", pe_cache), ("W_uv", W_uv)])
+    _check(q_absorbed.dim() == 4, f"q_absorbed must be [B,Sq,H,kv_rank] (got {tuple(q_absorbed.shape)})")
+    B, Sq, H, R = q_absorbed.shape
+    _check(q_rope.dim() == 4 and tuple(q_rope.shape[:3]) == (B, Sq, H),
+           f"q_rope must be [B,Sq,H,rope] (got {tuple(q_rope.shape)})")
+    D = q_rope.shape[3]
+    _check(c_kv.dim() == 3 and c_kv.shape[0] == B and c_kv.shape[2] == R,
+           f"c_kv must be [B,Sk,kv_rank] (got {tuple(c_kv.shape)})")
+    Sk = c_kv.shape[1]
+    _check(tuple(pe_cache.shape) == (B, Sk, D), f"pe_cache must be [B,Sk,rope] (got {tuple(pe_cache.shape)})")
+    _check(W_uv.dim() == 3 and W_uv.shape[0] == H and W_uv.shape[2] == R,
+           f"W_uv must be [H,v_dim,kv_rank] (got {tuple(W_uv.shape)})")
+    V = W_uv.shape[1]
+    qa, qr, ck, pe, wv = (t.contiguous() for t in (q_absorbed, q_rope, c_kv, pe_cache, W_uv))
+    out = torch.empty((B, Sq, H, V), dtype=dtype, device=device)
+    dt, pc = _DTYPE_CODES[dtype], _prec_code(precision)
+    nbytes = _c_size(0)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_attention_workspace_size(dt, pc, B, Sq, Sk, H, R, D, V, int(bool(causal)),
+                                                        ctypes.byref(nbytes)), "mla_attention")
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=device)
+        stream = torch.cuda.current_stream(device).cuda_stream
+        st = _lib.mla_attention(dt, pc, qa.data_ptr(), qr.data_ptr(), ck.data_ptr(), pe.data_ptr(),
+                                wv.data_ptr(), B, Sq, Sk, H, R, D, V, float(scale), int(bool(causal)),
+                                out.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    _raise_status(st, "mla_attention")
+    return out
+
+
+def mla_attention(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float) -> torch.Tensor:
+    """Kernel 3 — absorbed MLA: scores -> softmax -> ctx @ c_kv -> @ W_uv.
+
+    Same contract as the reference (mla_kernels.cu:1479-1682): scores are
+    divided by ``scale`` (sqrt(192) in the reference's callers); returns a new
+    [B,Sq,H,v_dim] tensor in the input dtype.
+    """
+    return mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale)
