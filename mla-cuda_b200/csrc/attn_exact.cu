@@ -20,6 +20,8 @@
 #include "qprep.cuh"
 #include "simt_gemm.cuh"
 
+#include <type_traits>
+
 namespace mla {
 namespace {
 
@@ -202,8 +204,11 @@ __global__ void __launch_bounds__(256) out_kernel(
     const int64_t m0 = int64_t(blockIdx.y) * Cfg::BM;
     for (int i = threadIdx.x; i < Cfg::BM; i += blockDim.x) {
         Acc l = Acc(0);
-        if (m0 + i < M)
+        if (l_part == nullptr) {
+            l = Acc(1);   // context already normalised
+        } else if (m0 + i < M) {
             for (int z = 0; z < splits; ++z) l += l_part[int64_t(z) * rows_total + (m0 + i) * heads + h];
+        }
         inv_l_s[i] = (l > Acc(0)) ? Acc(1) / l : Acc(0);
     }
     __syncthreads();
@@ -319,6 +324,24 @@ mla_status_t run_out(const AArgs& a, const APlan& p, const typename Cfg::Acc* O,
 }
 
 }  // namespace
+
+// Step 3d alone, from a context that is already normalised ([B*Sq*H, kv_rank]
+// fp32); used after the tensor-core attention's segment combine.
+template <typename T>
+mla_status_t attn_out_normalized(const AArgs& a, const float* O, cudaStream_t st) {
+    APlan p{};
+    p.rows_total = a.batch * a.sq * a.heads;
+    p.splits = 1;
+    if constexpr (std::is_same<acc_t<T>, float>::value) {
+        if (a.batch * a.sq <= 16) return run_out<CfgSmall<float>, T>(a, p, O, nullptr, st);
+        return run_out<CfgBig<float>, T>(a, p, O, nullptr, st);
+    } else {
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: fp32 context with fp64 storage");
+    }
+}
+template mla_status_t attn_out_normalized<float>(const AArgs&, const float*, cudaStream_t);
+template mla_status_t attn_out_normalized<__half>(const AArgs&, const float*, cudaStream_t);
+template mla_status_t attn_out_normalized<__nv_bfloat16>(const AArgs&, const float*, cudaStream_t);
 
 template <typename T>
 size_t attn_exact_workspace(const AArgs& a) { return make_plan<T>(a).total; }

@@ -1,13 +1,663 @@
-// Tensor-core attention path (placeholder until the tcgen05 kernel lands).
+// Tensor-core absorbed-MLA decode attention for sm_100a (MLA_PREC_TENSOR).
+//
+// Semantics: the reference's steps 3a-3c (mla_kernels.cu:808-1326, PyTorch
+// path exhaustive_benchmark_suite.py:289-304) fused into one persistent
+// flash-decode kernel, then an LSE combine of key segments and the W_uv
+// up-projection (3d, mla_kernels.cu:1339-1476). Scores never reach memory.
+//
+// Work unit. A "group" is one (b, q): the 128 heads of query q of sequence b,
+// which share the keys of sequence b. Each group is cut into 32-key tiles; all
+// tiles of all groups are laid end to end and split evenly over the persistent
+// clusters (stream-K), so every SM gets the same number of key tiles whatever
+// B and Sk are. A cluster's tiles of one group form a "segment"; each segment
+// leaves an unnormalised partial output plus its (max, sum) for the combine.
+//
+// Cluster of two CTAs (one per SM). The 512 latent dims are split between
+// them: CTA r owns c_kv dims [256r, 256r+256) and CTA 1 also the 64 rope dims.
+// Per key tile each CTA
+//   * loads only its own dims of the tile (TMA), once from HBM;
+//   * computes a partial score S_r = Q[:, dims_r] . K[:, dims_r]^T on the
+//     tensor cores (M = 128 heads, N = 32 keys, K = 256 or 320) into TMEM;
+//   * swaps S_r with its peer through distributed shared memory, so both
+//     hold S = S_0 + S_1 bit-identically and run the same online softmax;
+//   * accumulates its half of the context, O_r += P . V[:, 256r:256r+256]
+//     (M = 128, N = 256, K = 32) in TMEM. The same shared-memory tile is the
+//     K-major B operand of the score MMA and the MN-major B operand of P.V.
+// TMEM per CTA: O half 256 columns, two score/probability buffers of 32, the
+// bf16 query slice 128 or 160 (A operand read from TMEM).
+//
+// Operands are bf16 (fp16 for fp16 storage) with fp32 accumulation. fp32
+// storage is converted to bf16 in shared memory after the TMA load, so HBM
+// traffic stays one read of the fp32 cache.
+//
+// Warp roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
+// owner, warps 4-7 softmax (thread i <-> TMEM lane i <-> head i), warps 8-11
+// fp32->bf16 converters (fp32 storage only).
 #include "tc.cuh"
+#include "sm100.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <type_traits>
 
 namespace mla {
 
-bool tc_attention_supported(const AArgs&) { return false; }
-template <typename T> size_t tc_attention_workspace(const AArgs&) { return 0; }
-template <typename T> mla_status_t tc_attention(const AArgs&, cudaStream_t) {
-    return set_error(MLA_ERR_UNSUPPORTED, "MLA: tensor-core attention not built");
+// Runs steps 3d from a normalised context (defined in attn_exact.cu).
+template <typename T> mla_status_t attn_out_normalized(const AArgs& a, const float* O, cudaStream_t st);
+
+namespace tc {
+
+using namespace sm100;
+
+constexpr int NK = 32;                    // keys per tile
+constexpr int kHeads = 128;
+constexpr int kRank = 512;
+constexpr int kRope = 64;
+constexpr int kHalf = 256;                // latent dims per CTA
+constexpr int kThreads = 384;
+constexpr int kChunkBytes = NK * 128;     // one 64-dim chunk of a tile (128-byte rows)
+constexpr int kSlotBytes = 5 * kChunkBytes;
+constexpr int kStgBytes = NK * (kHalf + kRope) * 4;   // fp32 staging (c_kv half + pe)
+constexpr int kXStride = NK + 4;          // floats per exchange row (padded)
+constexpr int kXBytes = kHeads * kXStride * 4;
+
+// TMEM columns
+constexpr uint32_t kTmemO = 0;
+constexpr uint32_t kTmemS = 256;          // two buffers of NK columns
+constexpr uint32_t kTmemQ = 256 + 2 * NK; // up to 160 columns
+constexpr uint32_t kTmemCols = 512;
+
+enum : int { ERR_TIMEOUT_BASE = 100 };
+
+template <typename T> struct Traits;
+template <> struct Traits<float> {
+    static constexpr bool kConvert = true;  static constexpr int kSlots = 2; static constexpr int kStages = 3;
+    static constexpr uint32_t kFmt = 1;     // bf16 operands
+};
+template <> struct Traits<__nv_bfloat16> {
+    static constexpr bool kConvert = false; static constexpr int kSlots = 6; static constexpr int kStages = 0;
+    static constexpr uint32_t kFmt = 1;
+};
+template <> struct Traits<__half> {
+    static constexpr bool kConvert = false; static constexpr int kSlots = 6; static constexpr int kStages = 0;
+    static constexpr uint32_t kFmt = 0;     // fp16 operands
+};
+
+template <typename T>
+constexpr size_t smem_bytes() {
+    return 1024 /*align slack*/ + size_t(Traits<T>::kSlots) * kSlotBytes + size_t(Traits<T>::kStages) * kStgBytes +
+           2 * size_t(kXBytes) + 1024 /*barriers*/;
 }
+
+struct Params {
+    const void* qa;     // [B*Sq*H, 512]
+    const void* qr;     // [B*Sq*H, 64]
+    float* O_part;      // [slots, 128, 512]
+    float* ml;          // [slots, 128, 2]  (running max in log2 units, sum)
+    int* err;
+    int64_t batch, sq, sk;
+    int causal;
+    float c_log2;       // log2(e) / scale
+    int64_t total_tiles, tiles_per_cluster;
+    int max_segs;
+};
+
+// Key tiles of group g = (b, q).
+__device__ __forceinline__ int64_t group_keys(const Params& p, int64_t g) {
+    if (!p.causal) return p.sk;
+    const int64_t q = g % p.sq;
+    return p.sk - p.sq + q + 1;
+}
+__device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
+    return (group_keys(p, g) + NK - 1) / NK;
+}
+
+struct TileIter {
+    int64_t g, j, tiles, keys;
+};
+
+// Locates global tile index t: returns the group and the tile inside it.
+__device__ __forceinline__ TileIter locate(const Params& p, int64_t t) {
+    int64_t per_batch = 0;
+    for (int64_t q = 0; q < p.sq; ++q) per_batch += group_tiles(p, q);
+    const int64_t b = t / per_batch;
+    int64_t r = t % per_batch;
+    int64_t q = 0;
+    while (true) {
+        const int64_t n = group_tiles(p, b * p.sq + q);
+        if (r < n) break;
+        r -= n;
+        ++q;
+    }
+    TileIter it;
+    it.g = b * p.sq + q;
+    it.j = r;
+    it.keys = group_keys(p, it.g);
+    it.tiles = (it.keys + NK - 1) / NK;
+    return it;
+}
+__device__ __forceinline__ void advance(const Params& p, TileIter& it) {
+    if (++it.j == it.tiles) {
+        ++it.g;
+        it.j = 0;
+        it.keys = group_keys(p, it.g);
+        it.tiles = (it.keys + NK - 1) / NK;
+    }
+}
+
+struct Bars {
+    uint64_t full[6];       // tile data landed (TMA) - slots (16-bit) or stages (fp32)
+    uint64_t stg_empty[3];  // fp32 staging consumed by the converters
+    uint64_t bf_full[6];    // fp32: converted slot ready
+    uint64_t bf_empty[6];   // slot released by the P.V MMA
+    uint64_t s_full[2];
+    uint64_t p_full[2];
+    uint64_t o_done[2];
+    uint64_t x_full[2];     // peer's partial scores arrived
+    uint64_t q_ready;
+    uint32_t tmem_base;
+    int abort;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_ckv, const __grid_constant__ CUtensorMap tm_pe, const Params p)
+{
+    using Tr = Traits<T>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* slots = smem;
+    unsigned char* stg = slots + Tr::kSlots * kSlotBytes;
+    float* xbuf = reinterpret_cast<float*>(stg + Tr::kStages * kStgBytes);
+    Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<unsigned char*>(xbuf) + 2 * kXBytes);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t peer = rank ^ 1u;
+    const int dims = rank == 0 ? kHalf : kHalf + kRope;   // score dims of this CTA
+    const int64_t cl = cluster_id_x();
+    const int64_t t_begin = cl * p.tiles_per_cluster;
+    const int64_t t_end = min(t_begin + p.tiles_per_cluster, p.total_tiles);
+    volatile int* abort = &bars->abort;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 6; ++i) {
+            mbar_init(&bars->full[i], 1);
+            mbar_init(&bars->bf_full[i], 128);
+            mbar_init(&bars->bf_empty[i], 1);
+        }
+        for (int i = 0; i < 3; ++i) mbar_init(&bars->stg_empty[i], 128);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->s_full[i], 1);
+            mbar_init(&bars->p_full[i], 128);
+            mbar_init(&bars->o_done[i], 1);
+            mbar_init(&bars->x_full[i], 128);
+        }
+        mbar_init(&bars->q_ready, 128);
+        bars->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(&bars->tmem_base, kTmemCols);
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tm_ckv);
+        tma_prefetch_desc(&tm_pe);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    cluster_sync();   // the peer's barriers exist before any remote arrive
+    const uint32_t tmem = bars->tmem_base;
+
+    if (t_begin < t_end) {
+        if (warp == 0 && lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            TileIter it = locate(p, t_begin);
+            const uint32_t bytes = uint32_t(NK) * dims * sizeof(T);
+            for (int64_t i = 0; t_begin + i < t_end; ++i, advance(p, it)) {
+                const int32_t row = int32_t((it.g / p.sq) * p.sk + it.j * NK);
+                if constexpr (Tr::kConvert) {
+                    const int st = int(i % Tr::kStages);
+                    if (!mbar_wait(&bars->stg_empty[st], uint32_t(((i / Tr::kStages) & 1) ^ 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 1)) break;
+                    unsigned char* dst = stg + st * kStgBytes;
+                    mbar_arrive_expect_tx(&bars->full[st], bytes);
+                    tma_load_2d(dst, &tm_ckv, &bars->full[st], int32_t(rank * kHalf), row);
+                    if (rank == 1) tma_load_2d(dst + NK * kHalf * 4, &tm_pe, &bars->full[st], 0, row);
+                } else {
+                    const int sl = int(i % Tr::kSlots);
+                    if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 2)) break;
+                    unsigned char* dst = slots + sl * kSlotBytes;
+                    mbar_arrive_expect_tx(&bars->full[sl], bytes);
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_2d(dst + c * kChunkBytes, &tm_ckv, &bars->full[sl], int32_t(rank * kHalf + c * 64), row);
+                    if (rank == 1) tma_load_2d(dst + 4 * kChunkBytes, &tm_pe, &bars->full[sl], 0, row);
+                }
+            }
+        } else if (warp == 1) {
+            // ------------------------------------------------------------ MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t idesc_s = instr_desc(Tr::kFmt, 128, NK, 0, 0);
+                constexpr uint32_t idesc_o = instr_desc(Tr::kFmt, 128, kHalf, 0, 1);
+                const uint32_t smem_slots = smem_u32(slots);
+                TileIter it = locate(p, t_begin);
+                int64_t seg = 0;
+                bool ok = true;
+                auto issue_pv = [&](int64_t i, bool first) -> bool {
+                    const int sb = int(i & 1);
+                    if (!mbar_wait(&bars->p_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3))
+                        return false;
+                    tc_fence_after();
+                    const int sl = int(i % Tr::kSlots);
+                    const uint32_t base = smem_slots + sl * kSlotBytes;
+                    const uint32_t p_tmem = tmem + kTmemS + sb * NK;
+                    for (int k = 0; k < NK / 16; ++k) {
+                        // B = V [16 keys x 256 latent], MN-major, 128B swizzle:
+                        // LBO = stride between 64-dim chunks, SBO = stride between 8-key groups.
+                        const uint64_t bd = smem_desc(base + k * 16 * 128, kChunkBytes, 1024, 2);
+                        mma_ts(tmem + kTmemO, p_tmem + k * 8, bd, idesc_o, (first && k == 0) ? 0u : 1u);
+                    }
+                    mma_commit(&bars->bf_empty[sl]);
+                    mma_commit(&bars->o_done[sb]);
+                    return true;
+                };
+                for (int64_t i = 0; t_begin + i < t_end && ok; ++i) {
+                    const bool first = (i == 0) || it.j == 0;
+                    const bool last = (t_begin + i + 1 == t_end) || (it.j + 1 == it.tiles);
+                    if (first) {
+                        if (!mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)) break;
+                        ++seg;
+                    }
+                    const int sl = int(i % Tr::kSlots);
+                    uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
+                    if (!mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)) break;
+                    tc_fence_after();
+                    const uint32_t base = smem_slots + sl * kSlotBytes;
+                    const int sb = int(i & 1);
+                    for (int k = 0; k < dims / 16; ++k) {
+                        // B = K [32 keys x 16 dims], K-major, 128B swizzle: chunk k/4, +32 B per k-step.
+                        const uint64_t bd = smem_desc(base + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024, 2);
+                        mma_ts(tmem + kTmemS + sb * NK, tmem + kTmemQ + k * 8, bd, idesc_s, k > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&bars->s_full[sb]);
+                    if (!first) ok = issue_pv(i - 1, /*first=*/(i - 1 == 0) || it.j == 1);
+                    if (ok && last) ok = issue_pv(i, first);
+                    advance(p, it);
+                }
+            }
+        } else if (warp >= 4 && warp < 8) {
+            // ------------------------------------------------------------ softmax
+            const int row = threadIdx.x - 128;               // head
+            const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+            const float c = p.c_log2;
+            const float tau = 8.0f / c;                      // lazy rescale threshold (raw units)
+            float* xrow[2] = {xbuf + row * kXStride, xbuf + kHeads * kXStride + row * kXStride};
+            const uint32_t xpeer[2] = {map_peer(xrow[0], peer), map_peer(xrow[1], peer)};
+            TileIter it = locate(p, t_begin);
+            int64_t seg_local = 0;
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int64_t i = 0; t_begin + i < t_end; ++i, advance(p, it)) {
+                const bool first = (i == 0) || it.j == 0;
+                const bool last = (t_begin + i + 1 == t_end) || (it.j + 1 == it.tiles);
+                const int sb = int(i & 1);
+                if (first) {
+                    // load this group's query slice into TMEM as bf16/fp16 pairs
+                    const int64_t grow = it.g * kHeads + row;
+                    const T* qa = static_cast<const T*>(p.qa) + grow * kRank + rank * kHalf;
+                    for (int c32 = 0; c32 < kHalf / 64; ++c32) {
+                        uint32_t r[32];
+                        for (int e = 0; e < 32; ++e) {
+                            const float lo = cvt<float>(qa[c32 * 64 + 2 * e]);
+                            const float hi = cvt<float>(qa[c32 * 64 + 2 * e + 1]);
+                            if constexpr (Tr::kFmt == 0) {
+                                __half2 h2 = __floats2half2_rn(lo, hi);
+                                r[e] = *reinterpret_cast<uint32_t*>(&h2);
+                            } else {
+                                r[e] = pack_bf16(lo, hi);
+                            }
+                        }
+                        tmem_st32(tmem + lane_off + kTmemQ + c32 * 32, r);
+                    }
+                    if (rank == 1) {
+                        const T* qr = static_cast<const T*>(p.qr) + grow * kRope;
+                        uint32_t r[32];
+                        for (int e = 0; e < 32; ++e) {
+                            const float lo = cvt<float>(qr[2 * e]), hi = cvt<float>(qr[2 * e + 1]);
+                            if constexpr (Tr::kFmt == 0) {
+                                __half2 h2 = __floats2half2_rn(lo, hi);
+                                r[e] = *reinterpret_cast<uint32_t*>(&h2);
+                            } else {
+                                r[e] = pack_bf16(lo, hi);
+                            }
+                        }
+                        tmem_st32(tmem + lane_off + kTmemQ + 128, r);
+                    }
+                    tmem_st_wait();
+                    tc_fence_before();
+                    mbar_arrive(&bars->q_ready);
+                    m_run = -INFINITY;
+                    l_run = 0.f;
+                }
+                if (!mbar_wait(&bars->s_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 6)) break;
+                tc_fence_after();
+                uint32_t sr[32];
+                tmem_ld32(tmem + lane_off + kTmemS + sb * NK, sr);
+                tmem_ld_wait();
+                // send my partial scores to the peer, receive its partial
+                for (int e = 0; e < NK; e += 4)
+                    st_cluster_v4(xpeer[sb] + e * 4, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]),
+                                  __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
+                mbar_arrive_remote(&bars->x_full[sb], peer);
+                if (!mbar_wait(&bars->x_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 7,
+                               /*cluster_scope=*/true)) break;
+                float s[NK];
+                const int64_t key0 = it.j * NK;
+                float mt = -INFINITY;
+                for (int e = 0; e < NK; e += 4) {
+                    const float4 pv = *reinterpret_cast<const float4*>(xrow[sb] + e);
+                    s[e] = __uint_as_float(sr[e]) + pv.x;
+                    s[e + 1] = __uint_as_float(sr[e + 1]) + pv.y;
+                    s[e + 2] = __uint_as_float(sr[e + 2]) + pv.z;
+                    s[e + 3] = __uint_as_float(sr[e + 3]) + pv.w;
+                }
+                for (int e = 0; e < NK; ++e) {
+                    if (key0 + e >= it.keys) s[e] = -INFINITY;
+                    mt = fmaxf(mt, s[e]);
+                }
+                if (first) {
+                    m_run = mt;
+                } else if (mt > m_run + tau) {
+                    // rescale the running output once P.V of the previous tile has landed
+                    const int pb = int((i - 1) & 1);
+                    if (!mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) >> 1) & 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 8)) break;
+                    tc_fence_after();
+                    const float alpha = ex2((m_run - mt) * c);
+                    for (int c32 = 0; c32 < kHalf / 32; ++c32) {
+                        uint32_t o[32];
+                        tmem_ld32(tmem + lane_off + kTmemO + c32 * 32, o);
+                        tmem_ld_wait();
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+                        tmem_st32(tmem + lane_off + kTmemO + c32 * 32, o);
+                    }
+                    tmem_st_wait();
+                    l_run *= alpha;
+                    m_run = mt;
+                }
+                const float mc = m_run * c;
+                uint32_t pk[NK / 2];
+                float ls = 0.f;
+                for (int e = 0; e < NK; e += 2) {
+                    const float p0 = ex2(fmaf(s[e], c, -mc));
+                    const float p1 = ex2(fmaf(s[e + 1], c, -mc));
+                    ls += p0 + p1;
+                    if constexpr (Tr::kFmt == 0) {
+                        __half2 h2 = __floats2half2_rn(p0, p1);
+                        pk[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+                    } else {
+                        pk[e / 2] = pack_bf16(p0, p1);
+                    }
+                }
+                l_run += ls;
+                tmem_st16(tmem + lane_off + kTmemS + sb * NK, pk);
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&bars->p_full[sb]);
+                if (last) {
+                    if (!mbar_wait(&bars->o_done[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 9))
+                        break;
+                    tc_fence_after();
+                    const int64_t slot = cl * p.max_segs + seg_local;
+                    float* dst = p.O_part + (slot * kHeads + row) * kRank + rank * kHalf;
+                    for (int c32 = 0; c32 < kHalf / 32; ++c32) {
+                        uint32_t o[32];
+                        tmem_ld32(tmem + lane_off + kTmemO + c32 * 32, o);
+                        tmem_ld_wait();
+                        float4* d4 = reinterpret_cast<float4*>(dst + c32 * 32);
+                        for (int e = 0; e < 8; ++e)
+                            d4[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                                __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+                    }
+                    if (rank == 0) {
+                        p.ml[(slot * kHeads + row) * 2] = m_run * c;
+                        p.ml[(slot * kHeads + row) * 2 + 1] = l_run;
+                    }
+                    tc_fence_before();
+                    ++seg_local;
+                }
+            }
+        } else if (warp >= 8 && Tr::kConvert) {
+            // ------------------------------------------------------------ fp32 -> bf16
+            const int ct = threadIdx.x - 256;
+            for (int64_t i = 0; t_begin + i < t_end; ++i) {
+                const int st = int(i % Tr::kStages), sl = int(i % Tr::kSlots);
+                if (!mbar_wait(&bars->full[st], uint32_t((i / Tr::kStages) & 1), abort, p.err, ERR_TIMEOUT_BASE + 10))
+                    break;
+                if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                               ERR_TIMEOUT_BASE + 11)) break;
+                const float* src = reinterpret_cast<const float*>(stg + st * kStgBytes);
+                unsigned char* dst = slots + sl * kSlotBytes;
+                // c_kv half: NK rows x 256 floats = NK*32 units of 8 floats
+                for (int u = ct; u < NK * 32; u += 128) {
+                    const int r = u >> 5, c8 = u & 31;
+                    const float4 a = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8);
+                    const float4 b = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8 + 4);
+                    uint4 v;
+                    v.x = pack_bf16(a.x, a.y); v.y = pack_bf16(a.z, a.w);
+                    v.z = pack_bf16(b.x, b.y); v.w = pack_bf16(b.z, b.w);
+                    const int chunk = c8 >> 3, unit = (c8 & 7) ^ (r & 7);
+                    *reinterpret_cast<uint4*>(dst + chunk * kChunkBytes + r * 128 + unit * 16) = v;
+                }
+                if (rank == 1) {
+                    const float* pe = src + NK * kHalf;
+                    for (int u = ct; u < NK * 8; u += 128) {
+                        const int r = u >> 3, c8 = u & 7;
+                        const float4 a = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8);
+                        const float4 b = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8 + 4);
+                        uint4 v;
+                        v.x = pack_bf16(a.x, a.y); v.y = pack_bf16(a.z, a.w);
+                        v.z = pack_bf16(b.x, b.y); v.w = pack_bf16(b.z, b.w);
+                        const int unit = c8 ^ (r & 7);
+                        *reinterpret_cast<uint4*>(dst + 4 * kChunkBytes + r * 128 + unit * 16) = v;
+                    }
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&bars->bf_full[sl]);
+                mbar_arrive(&bars->stg_empty[st]);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (bars->abort) {
+        // let in-flight asynchronous copies and MMAs drain before freeing resources
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) { }
+    }
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+    cluster_sync();
+}
+
+// Combine the segments of every (group, head) row into a normalised context.
+// One warp per row; the cluster segments covering group g are contiguous.
+__global__ void __launch_bounds__(256) combine_kernel(const Params p, float* __restrict__ O_norm, int64_t groups)
+{
+    const int64_t rowid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (rowid >= groups * kHeads) return;
+    const int64_t g = rowid / kHeads, h = rowid % kHeads;
+    // first global tile of g
+    int64_t per_batch = 0;
+    for (int64_t q = 0; q < p.sq; ++q) per_batch += group_tiles(p, q);
+    const int64_t b = g / p.sq, qg = g % p.sq;
+    int64_t t0 = b * per_batch;
+    for (int64_t q = 0; q < qg; ++q) t0 += group_tiles(p, b * p.sq + q);
+    const int64_t t1 = t0 + group_tiles(p, g);   // exclusive
+    const int64_t c0 = t0 / p.tiles_per_cluster, c1 = (t1 - 1) / p.tiles_per_cluster;
+    float M = -INFINITY;
+    for (int64_t c = c0; c <= c1; ++c) {
+        const int64_t g0 = locate(p, c * p.tiles_per_cluster).g;
+        const int64_t slot = c * p.max_segs + (g - g0);
+        M = fmaxf(M, p.ml[(slot * kHeads + h) * 2]);
+    }
+    float acc[16];
+    for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+    float L = 0.f;
+    for (int64_t c = c0; c <= c1; ++c) {
+        const int64_t g0 = locate(p, c * p.tiles_per_cluster).g;
+        const int64_t slot = c * p.max_segs + (g - g0);
+        const float w = exp2f(p.ml[(slot * kHeads + h) * 2] - M);
+        L += w * p.ml[(slot * kHeads + h) * 2 + 1];
+        const float* src = p.O_part + (slot * kHeads + h) * kRank;
+        for (int e = 0; e < 16; ++e) acc[e] += w * src[e * 32 + lane];
+    }
+    const float inv = 1.f / L;
+    float* dst = O_norm + rowid * kRank;
+    for (int e = 0; e < 16; ++e) dst[e * 32 + lane] = acc[e] * inv;
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+template <typename T>
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint32_t box_cols, bool swz) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const CUtensorMapDataType dt = std::is_same<T, float>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : std::is_same<T, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                  : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(cols) * sizeof(T)};
+    cuuint32_t box[2] = {box_cols, cuuint32_t(NK)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+struct Plan {
+    int64_t groups, total_tiles, tiles_per_cluster, nclusters;
+    int max_segs;
+    size_t off_err, off_O, off_ml, off_norm, total;
+};
+
+int64_t tiles_of(const AArgs& a, int64_t q) {
+    const int64_t k = a.causal ? a.sk - a.sq + q + 1 : a.sk;
+    return (k + NK - 1) / NK;
+}
+
+Plan make_plan(const AArgs& a) {
+    Plan pl{};
+    pl.groups = a.batch * a.sq;
+    int64_t per_batch = 0, min_tiles = INT64_MAX;
+    for (int64_t q = 0; q < a.sq; ++q) {
+        const int64_t n = tiles_of(a, q);
+        per_batch += n;
+        min_tiles = n < min_tiles ? n : min_tiles;
+    }
+    pl.total_tiles = per_batch * a.batch;
+    int64_t ncl = sm_count() / 2;
+    if (ncl < 1) ncl = 1;
+    if (ncl > pl.total_tiles) ncl = pl.total_tiles;
+    pl.tiles_per_cluster = (pl.total_tiles + ncl - 1) / ncl;
+    pl.nclusters = (pl.total_tiles + pl.tiles_per_cluster - 1) / pl.tiles_per_cluster;
+    pl.max_segs = int((pl.tiles_per_cluster + min_tiles - 1) / min_tiles + 1);
+    const int64_t slots = pl.nclusters * pl.max_segs;
+    size_t off = 0;
+    pl.off_err = off;  off = align_up(off + 256, 256);
+    pl.off_O = off;    off = align_up(off + size_t(slots) * kHeads * kRank * 4, 256);
+    pl.off_ml = off;   off = align_up(off + size_t(slots) * kHeads * 2 * 4, 256);
+    pl.off_norm = off; off = align_up(off + size_t(pl.groups) * kHeads * kRank * 4, 256);
+    pl.total = off;
+    return pl;
+}
+
+}  // namespace tc
+
+bool tc_attention_supported(const AArgs& a) {
+    return a.heads == tc::kHeads && a.kv_rank == tc::kRank && a.rope == tc::kRope && a.sk > 0 &&
+           a.batch * a.sk < (int64_t(1) << 31);
+}
+
+template <typename T>
+size_t tc_attention_workspace(const AArgs& a) {
+    if constexpr (std::is_same<T, double>::value) return 0;
+    else return tc::make_plan(a).total;
+}
+
+template <typename T>
+mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
+    if constexpr (std::is_same<T, double>::value) {
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: tensor-core attention has no fp64 variant");
+    } else {
+        using namespace tc;
+        const Plan pl = make_plan(a);
+        char* ws = static_cast<char*>(a.workspace);
+        Params p{};
+        p.qa = a.q_absorbed;
+        p.qr = a.q_rope;
+        p.O_part = reinterpret_cast<float*>(ws + pl.off_O);
+        p.ml = reinterpret_cast<float*>(ws + pl.off_ml);
+        p.err = reinterpret_cast<int*>(ws + pl.off_err);
+        p.batch = a.batch; p.sq = a.sq; p.sk = a.sk; p.causal = a.causal;
+        p.c_log2 = float(1.4426950408889634 / a.scale);
+        p.total_tiles = pl.total_tiles;
+        p.tiles_per_cluster = pl.tiles_per_cluster;
+        p.max_segs = pl.max_segs;
+        float* O_norm = reinterpret_cast<float*>(ws + pl.off_norm);
+
+        CUtensorMap tm_ckv, tm_pe;
+        const bool swz = !Traits<T>::kConvert;
+        const int64_t rows = a.batch * a.sk;
+        if (!make_map<T>(&tm_ckv, a.c_kv, rows, kRank, swz ? 64 : kHalf, swz) ||
+            !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, 64, swz))
+            return set_error(MLA_ERR_CUDA, "MLA: cuTensorMapEncodeTiled failed (alignment of c_kv / pe_cache?)");
+
+        if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess)
+            return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
+        auto kern = mla_decode_tc_kernel<T>;
+        const size_t smem = smem_bytes<T>();
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(unsigned(2 * pl.nclusters), 1, 1);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p) != cudaSuccess) {
+            cudaGetLastError();
+            return set_error(MLA_ERR_CUDA, "MLA: launch of the tensor-core attention kernel failed");
+        }
+        MLA_TRY(check_launch("tensor-core attention"));
+        const int64_t rows_total = pl.groups * kHeads;
+        combine_kernel<<<unsigned((rows_total * 32 + 255) / 256), 256, 0, st>>>(p, O_norm, pl.groups);
+        MLA_TRY(check_launch("segment combine"));
+        return attn_out_normalized<T>(a, O_norm, st);
+    }
+}
+
 template size_t tc_attention_workspace<float>(const AArgs&);
 template size_t tc_attention_workspace<double>(const AArgs&);
 template size_t tc_attention_workspace<__half>(const AArgs&);
