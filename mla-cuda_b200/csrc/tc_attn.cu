@@ -40,6 +40,10 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <unistd.h>
 #include <type_traits>
 
 namespace mla {
@@ -97,6 +101,7 @@ struct Params {
     float* O_part;      // [slots, 128, 512]
     float* ml;          // [slots, 128, 2]  (running max in log2 units, sum)
     int* err;
+    int* trace;         // debug only (MLA_TC_TRACE): per-CTA progress words in mapped host memory
     int64_t batch, sq, sk;
     int causal;
     float c_log2;       // log2(e) / scale
@@ -112,6 +117,13 @@ __device__ __forceinline__ int64_t group_keys(const Params& p, int64_t g) {
 }
 __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
     return (group_keys(p, g) + NK - 1) / NK;
+}
+
+__device__ __forceinline__ void trace_put(const Params& p, int role, int64_t v) {
+    if (p.trace) {
+        *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 8 + role) = int(v);
+        __threadfence_system();
+    }
 }
 
 struct TileIter {
@@ -217,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             const uint32_t bytes = uint32_t(NK) * dims * sizeof(T);
             for (int64_t i = 0; t_begin + i < t_end; ++i, advance(p, it)) {
                 const int32_t row = int32_t((it.g / p.sq) * p.sk + it.j * NK);
+                trace_put(p, 0, i * 16 + 1);
                 if constexpr (Tr::kConvert) {
                     const int st = int(i % Tr::kStages);
                     if (!mbar_wait(&bars->stg_empty[st], uint32_t(((i / Tr::kStages) & 1) ^ 1), abort, p.err,
@@ -271,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                         ++seg;
                     }
                     const int sl = int(i % Tr::kSlots);
+                    trace_put(p, 1, i * 16 + 1);
                     uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
                     if (!mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)) break;
                     tc_fence_after();
@@ -282,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                         mma_ts(tmem + kTmemS + sb * NK, tmem + kTmemQ + k * 8, bd, idesc_s, k > 0 ? 1u : 0u);
                     }
                     mma_commit(&bars->s_full[sb]);
+                    trace_put(p, 1, i * 16 + 2);
                     if (!first) ok = issue_pv(i - 1, /*first=*/(i - 1 == 0) || it.j == 1);
                     if (ok && last) ok = issue_pv(i, first);
                     advance(p, it);
@@ -303,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 const bool last = (t_begin + i + 1 == t_end) || (it.j + 1 == it.tiles);
                 const int sb = int(i & 1);
                 if (first) {
+                    __syncwarp();   // tcgen05.st below is warp-collective
                     // load this group's query slice into TMEM as bf16/fp16 pairs
                     const int64_t grow = it.g * kHeads + row;
                     const T* qa = static_cast<const T*>(p.qa) + grow * kRank + rank * kHalf;
@@ -340,7 +356,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     m_run = -INFINITY;
                     l_run = 0.f;
                 }
-                if (!mbar_wait(&bars->s_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 6)) break;
+                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 1);
+                // every lane polls, then the warp reconverges: the tcgen05.ld below is warp-collective
+                if (!__all_sync(0xffffffffu,
+                                mbar_wait(&bars->s_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 6)))
+                    break;
+                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 2);
                 tc_fence_after();
                 uint32_t sr[32];
                 tmem_ld32(tmem + lane_off + kTmemS + sb * NK, sr);
@@ -350,8 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     st_cluster_v4(xpeer[sb] + e * 4, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]),
                                   __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
                 mbar_arrive_remote(&bars->x_full[sb], peer);
-                if (!mbar_wait(&bars->x_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 7,
-                               /*cluster_scope=*/true)) break;
+                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 3);
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_full[sb], uint32_t((i >> 1) & 1), abort, p.err,
+                                                       ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true)))
+                    break;
                 float s[NK];
                 const int64_t key0 = it.j * NK;
                 float mt = -INFINITY;
@@ -368,12 +391,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 }
                 if (first) {
                     m_run = mt;
-                } else if (mt > m_run + tau) {
-                    // rescale the running output once P.V of the previous tile has landed
+                } else if (__any_sync(0xffffffffu, mt > m_run + tau)) {
+                    // Lazy rescale: the decision is per warp, because the TMEM accesses
+                    // below are warp-collective. Every lane of the warp moves to its own
+                    // new maximum (alpha <= 1). The peer CTA sees the same scores, so it
+                    // takes the same decision. Waits for P.V of the previous tile first.
                     const int pb = int((i - 1) & 1);
-                    if (!mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) >> 1) & 1), abort, p.err,
-                                   ERR_TIMEOUT_BASE + 8)) break;
+                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) >> 1) & 1), abort,
+                                                           p.err, ERR_TIMEOUT_BASE + 8)))
+                        break;
                     tc_fence_after();
+                    mt = fmaxf(mt, m_run);
                     const float alpha = ex2((m_run - mt) * c);
                     for (int c32 = 0; c32 < kHalf / 32; ++c32) {
                         uint32_t o[32];
@@ -401,12 +429,15 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     }
                 }
                 l_run += ls;
+                __syncwarp();
                 tmem_st16(tmem + lane_off + kTmemS + sb * NK, pk);
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
+                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 4);
                 if (last) {
-                    if (!mbar_wait(&bars->o_done[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 9))
+                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[sb], uint32_t((i >> 1) & 1), abort, p.err,
+                                                           ERR_TIMEOUT_BASE + 9)))
                         break;
                     tc_fence_after();
                     const int64_t slot = cl * p.max_segs + seg_local;
@@ -437,6 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     break;
                 if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
                                ERR_TIMEOUT_BASE + 11)) break;
+                if (ct == 0) trace_put(p, 3, i * 16 + 2);
                 const float* src = reinterpret_cast<const float*>(stg + st * kStgBytes);
                 unsigned char* dst = slots + sl * kSlotBytes;
                 // c_kv half: NK rows x 256 floats = NK*32 units of 8 floats
@@ -470,16 +502,21 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
         }
     }
 
+    if (threadIdx.x == 0) trace_put(p, 4, 1);
     tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) trace_put(p, 5, bars->abort ? 2 : 1);
     if (bars->abort) {
         // let in-flight asynchronous copies and MMAs drain before freeing resources
         const uint64_t t0 = globaltimer();
         while (globaltimer() - t0 < 2000000ull) { }
     }
     tc_fence_after();
+    __syncwarp();
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+    __syncwarp();
     cluster_sync();
+    if (threadIdx.x == 0) trace_put(p, 6, 1);
 }
 
 // Combine the segments of every (group, head) row into a normalised context.
@@ -573,6 +610,10 @@ Plan make_plan(const AArgs& a) {
     }
     pl.total_tiles = per_batch * a.batch;
     int64_t ncl = sm_count() / 2;
+    if (const char* e = getenv("MLA_TC_MAX_CLUSTERS")) {   // debug knob
+        const int64_t lim = atoll(e);
+        if (lim > 0 && lim < ncl) ncl = lim;
+    }
     if (ncl < 1) ncl = 1;
     if (ncl > pl.total_tiles) ncl = pl.total_tiles;
     pl.tiles_per_cluster = (pl.total_tiles + ncl - 1) / ncl;
@@ -646,11 +687,35 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
+        int* trace_host = nullptr;
+        if (getenv("MLA_TC_TRACE")) {   // debug: progress words polled from the host while the kernel runs
+            if (cudaHostAlloc(reinterpret_cast<void**>(&trace_host), 2 * 148 * 8 * sizeof(int), cudaHostAllocMapped) ==
+                cudaSuccess) {
+                memset(trace_host, 0xff, 2 * 148 * 8 * sizeof(int));
+                cudaHostGetDevicePointer(reinterpret_cast<void**>(&p.trace), trace_host, 0);
+            }
+        }
         if (cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p) != cudaSuccess) {
             cudaGetLastError();
             return set_error(MLA_ERR_CUDA, "MLA: launch of the tensor-core attention kernel failed");
         }
         MLA_TRY(check_launch("tensor-core attention"));
+        if (trace_host) {
+            cudaEvent_t ev;
+            cudaEventCreate(&ev);
+            cudaEventRecord(ev, st);
+            for (int k = 0; k < 100 && cudaEventQuery(ev) == cudaErrorNotReady; ++k) usleep(50000);
+            const bool done = cudaEventQuery(ev) == cudaSuccess;
+            fprintf(stderr, "[mla trace] kernel %s; grid %lld CTAs\n", done ? "finished" : "STILL RUNNING after 5 s",
+                    (long long)(2 * pl.nclusters));
+            for (int64_t b = 0; b < 2 * pl.nclusters && b < 296; ++b) {
+                const volatile int* t = trace_host + b * 8;
+                fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d\n", (long long)b,
+                        t[0], t[1], t[2], t[3], t[4], t[5], t[6]);
+            }
+            if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
+            cudaFreeHost(trace_host);
+        }
         const int64_t rows_total = pl.groups * kHeads;
         combine_kernel<<<unsigned((rows_total * 32 + 255) / 256), 256, 0, st>>>(p, O_norm, pl.groups);
         MLA_TRY(check_launch("segment combine"));
