@@ -45,10 +45,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=sorted(mc.CONFIGS))
-    ap.add_argument("--precision", default=None, choices=["exact", "tensor"])
+    ap.add_argument("--precision", default="tensor", choices=["exact", "tensor"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--min-warmup-s", type=float, default=1.5,
+                    help="minimum warm-up wall time (lets the clock sampler start); 0 under a profiler")
+    ap.add_argument("--no-stages", action="store_true", help="skip the per-stage / per-precision timings")
     return ap.parse_args()
 
 
@@ -99,7 +102,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -209,7 +212,7 @@ def main_ours(args):
     import mla_custom_cuda as mcc
 
     w = mc.CONFIGS[args.config]
-    precision = args.precision or "exact"
+    precision = args.precision
     B = w.batch
     t = mc.make_inputs(w, device=dev, gen="device", seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
@@ -218,14 +221,33 @@ def main_ours(args):
         if world > 1:
             torch.distributed.barrier()
 
-    # ---- device-resident timed region
-    for _ in range(max(args.warmup, 3)):
-        run_forward(mcc, t, w, precision)
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    # ---- device-resident timed region (whole layer forward, headline precision).
+    # The clock sampler starts before the warm-up, which runs for at least W steps
+    # and at least --min-warmup-s seconds so nvidia-smi samples a loaded GPU.
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        t_w = time.perf_counter()
+        n_w = 0
+        while n_w < max(args.warmup, 3) or time.perf_counter() - t_w < args.min_warmup_s:
+            run_forward(mcc, t, w, precision)
+            n_w += 1
+            if n_w % 8 == 0:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
         ev0.record(stream)
         for _ in range(args.steps):
             run_forward(mcc, t, w, precision)
@@ -241,30 +263,21 @@ def main_ours(args):
     tokens_total = B * w.sq * world
     value = tokens_total / (ms * 1e-3)
 
-    # ---- attention-stage timing for the roofline (same stream, events, inputs > L2)
-    qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
-                               w.nope, w.rope, mc.EPS, precision=precision)
-    for _ in range(3):
-        mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, causal=w.causal,
-                             precision=precision)
-    torch.cuda.synchronize()
+    # ---- per-stage timing (same stream, CUDA events; inputs larger than L2)
     n_att = max(5, args.steps)
-    ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ea.record(stream)
-    for _ in range(n_att):
-        mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, causal=w.causal,
-                             precision=precision)
-    eb.record(stream)
-    torch.cuda.synchronize()
-    att_ms = ea.elapsed_time(eb) / n_att
-    eq, er = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    eq.record(stream)
-    for _ in range(n_att):
-        mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
-                          w.nope, w.rope, mc.EPS, precision=precision)
-    er.record(stream)
-    torch.cuda.synchronize()
-    q_ms = eq.elapsed_time(er) / n_att
+    stages = {}
+    for prec in ((precision,) if args.no_stages else ("tensor", "exact")):
+        qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                                   w.nope, w.rope, mc.EPS, precision=prec)
+        att = timed(lambda: mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
+                                                 causal=w.causal, precision=prec), n_att)
+        qp = timed(lambda: mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
+                                             t["positions"], w.nope, w.rope, mc.EPS, precision=prec), n_att)
+        fwd = att + qp if prec != precision else ms
+        stages[prec] = {"q_absorbed_ms": qp, "mla_attention_ms": att, "layer_ms": fwd,
+                        "tokens_per_s": B * w.sq / (fwd * 1e-3)}
+    att_ms = stages[precision]["mla_attention_ms"]
+    q_ms = stages[precision]["q_absorbed_ms"]
 
     cache_b, weight_b, act_b = workload_bytes(w, B)
     qf, af = workload_flops(w, B)
@@ -317,17 +330,20 @@ def main_ours(args):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
-            "dtype": dtype_name if precision == "exact" else "bf16-tc",
+            "dtype": dtype_name if precision == "exact" else
+                     ("bf16" if w.dtype != torch.float16 else "f16") + " tensor-core operands, f32 accumulate, "
+                     + dtype_name + " storage",
             "data": "synthetic (seeded N(0,1) cache / activations, N(0,0.02) weights)",
             "config": {**w.describe(), "global_batch": B * world, "precision": precision,
                        "parallelism": f"batch-shard dp{world}",
                        "l2": "inputs larger than L2 (cache %.2f GB per GPU)" % (cache_b / 1e9)},
-            "stages_ms": {"q_absorbed": q_ms, "mla_attention": att_ms},
+            "stages": stages,
             "roofline": {"bound": "hbm", "kernel": "mla_attention (cache read)",
                          "achieved": att_gbs, "peak": hbm, "unit": "GB/s", "frac": att_gbs / hbm,
                          "traffic": None, "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": cache_b,
-                         "note": "exact path is CUDA-core FMA bound; tensor-core path is HBM bound"},
+                         "note": "mla_attention stage = fused tcgen05 decode kernel + segment combine + W_uv "
+                                 "projection; algorithmic bytes = c_kv + pe_cache read once"},
             "tflops": {"q_absorbed": qf / (q_ms * 1e-3) / 1e12, "mla_attention": af / (att_ms * 1e-3) / 1e12},
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,
