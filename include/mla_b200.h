@@ -146,6 +146,34 @@ MLA_API mla_status_t mla_attention(
     void* out,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------- allocation-free variant --
+ * No counterpart in the reference. Same computation as mla_attention with
+ * MLA_PREC_TENSOR (fp32, fp16 or bf16 storage; heads 128, kv_rank 512,
+ * rope 64), for callers that cannot allocate device memory when they call:
+ * a server whose memory pool already owns the GPU, or code running where
+ * cudaMalloc may not be called. The workspace is a fixed device array of
+ * mla_attention_noalloc_max_scratch() bytes (96 MiB) that exists on every
+ * GPU where the library is loaded, until the process exits; shapes that need
+ * more return MLA_ERR_WORKSPACE. Nothing is allocated or freed.
+ *
+ * The first call on a device looks up that array's device address (once per
+ * device, with the device current); make that first call before any stream
+ * capture. All calls share the one array and it keeps the last call's
+ * contents, so calls that overlap on the GPU (different streams or threads)
+ * race: serialise them.
+ */
+MLA_API mla_status_t mla_attention_noalloc(
+    mla_dtype_t dtype,
+    const void* q_absorbed, const void* q_rope,
+    const void* c_kv, const void* pe_cache, const void* W_uv,
+    int64_t batch, int64_t sq, int64_t sk, int64_t heads,
+    int64_t kv_rank, int64_t rope, int64_t v_dim,
+    double scale, int causal,
+    void* out, void* stream);
+
+/* Size in bytes of the fixed scratch array used by mla_attention_noalloc. */
+MLA_API size_t mla_attention_noalloc_max_scratch(void);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif
