@@ -30,6 +30,9 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "-I", str(INCLUDE), "-I", str(CSRC),
 ] + ARCH
+if os.environ.get("MLA_TC_PROFILE"):        # debug: per-wait cycle accounting in the tensor-core kernel
+    NVCC_FLAGS.append("-DMLA_TC_PROFILE")
+NVCC_FLAGS += os.environ.get("NVCC_EXTRA", "").split()     # debug / tuning defines
 
 
 def nvcc() -> str:

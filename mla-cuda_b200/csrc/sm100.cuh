@@ -136,6 +136,14 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, f
                  : "memory");
 }
 
+// Asynchronous 16-byte store into a peer CTA's shared memory that counts its
+// bytes on the peer's mbarrier (transaction count); the sender does not wait.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a, float b, float c, float d,
+                                            uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(remote_addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar) : "memory");
+}
+
 // ----------------------------------------------------------------- tcgen05
 // Allocation is warp-wide; the TMEM base address is written to *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {

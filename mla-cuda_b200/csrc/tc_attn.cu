@@ -23,16 +23,17 @@
 //   * accumulates its half of the context, O_r += P . V[:, 256r:256r+256]
 //     (M = 128, N = 256, K = 32) in TMEM. The same shared-memory tile is the
 //     K-major B operand of the score MMA and the MN-major B operand of P.V.
-// TMEM per CTA: O half 256 columns, two score/probability buffers of 32, the
-// bf16 query slice 128 or 160 (A operand read from TMEM).
+// TMEM per CTA: O half 256 columns, three score/probability buffers of 32, the
+// bf16 query slice 128 or 160 (A operand read from TMEM) - 512 columns in all.
 //
 // Operands are bf16 (fp16 for fp16 storage) with fp32 accumulation. fp32
 // storage is converted to bf16 in shared memory after the TMA load, so HBM
 // traffic stays one read of the fp32 cache.
 //
-// Warp roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
-// owner, warps 4-7 softmax (thread i <-> TMEM lane i <-> head i), warps 8-11
-// fp32->bf16 converters (fp32 storage only).
+// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
+// owner, warps 4-7 softmax (thread i <-> TMEM lane i <-> head i; a warp reaches
+// only TMEM lanes 32*(warp%4)..+31), warps 2, 3, 8, 9 fp32->bf16 converters
+// (fp32 storage only).
 #include "tc.cuh"
 #include "sm100.cuh"
 
@@ -60,24 +61,34 @@ constexpr int kHeads = 128;
 constexpr int kRank = 512;
 constexpr int kRope = 64;
 constexpr int kHalf = 256;                // latent dims per CTA
-constexpr int kThreads = 384;
+constexpr int kThreads = 320;
 constexpr int kChunkBytes = NK * 128;     // one 64-dim chunk of a tile (128-byte rows)
 constexpr int kSlotBytes = 5 * kChunkBytes;
-constexpr int kStgBytes = NK * (kHalf + kRope) * 4;   // fp32 staging (c_kv half + pe)
-constexpr int kXStride = NK + 4;          // floats per exchange row (padded)
-constexpr int kXBytes = kHeads * kXStride * 4;
+constexpr int kStgRows = NK / 2;          // an fp32 staging buffer holds half a key tile
+constexpr int kStgBytes = kStgRows * (kHalf + kRope) * 4;
+constexpr int kXBufs = 4;                 // partial-score exchange buffers (see the softmax role)
+constexpr int kXBytes = kHeads * NK * 4;  // one buffer: 128 rows x 32 fp32, 16-byte chunks XOR-swizzled by row
 
-// TMEM columns
+// TMEM columns: O half, kSBufs score / probability buffers, the query slice.
 constexpr uint32_t kTmemO = 0;
-constexpr uint32_t kTmemS = 256;          // two buffers of NK columns
-constexpr uint32_t kTmemQ = 256 + 2 * NK; // up to 160 columns
+constexpr int kSBufs = 3;
+constexpr uint32_t kTmemS = 256;
+constexpr uint32_t kTmemQ = 256 + kSBufs * NK;   // up to 160 columns, ends at column 512
 constexpr uint32_t kTmemCols = 512;
 
 enum : int { ERR_TIMEOUT_BASE = 100 };
 
+#ifndef MLA_TC_F32_SLOTS
+#define MLA_TC_F32_SLOTS 6
+#endif
+#ifndef MLA_TC_F32_STAGES
+#define MLA_TC_F32_STAGES 2
+#endif
 template <typename T> struct Traits;
 template <> struct Traits<float> {
-    static constexpr bool kConvert = true;  static constexpr int kSlots = 2; static constexpr int kStages = 3;
+    static constexpr bool kConvert = true;
+    static constexpr int kSlots = MLA_TC_F32_SLOTS;
+    static constexpr int kStages = MLA_TC_F32_STAGES;
     static constexpr uint32_t kFmt = 1;     // bf16 operands
 };
 template <> struct Traits<__nv_bfloat16> {
@@ -89,10 +100,15 @@ template <> struct Traits<__half> {
     static constexpr uint32_t kFmt = 0;     // fp16 operands
 };
 
+// Shared memory: kSlots 128B-swizzled 16-bit key tiles (the MMA operands),
+// kStages fp32 half-tile staging buffers (fp32 storage only), kXBufs exchange
+// buffers, barriers. 16-bit storage is loaded by TMA straight into the slots;
+// fp32 storage lands in staging, which the converter warps release as soon as
+// they have read it (so TMA keeps loads in flight), and is converted into slots.
 template <typename T>
 constexpr size_t smem_bytes() {
     return 1024 /*align slack*/ + size_t(Traits<T>::kSlots) * kSlotBytes + size_t(Traits<T>::kStages) * kStgBytes +
-           2 * size_t(kXBytes) + 1024 /*barriers*/;
+           kXBufs * size_t(kXBytes) + 1024 /*barriers*/;
 }
 
 struct Params {
@@ -120,11 +136,19 @@ __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
 }
 
 __device__ __forceinline__ void trace_put(const Params& p, int role, int64_t v) {
-    if (p.trace) {
-        *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 8 + role) = int(v);
-        __threadfence_system();
-    }
+    if (p.trace) *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 32 + role) = int(v);
 }
+
+// Debug wait accounting: cycles spent per wait site, compiled in only with
+// -DMLA_TC_PROFILE (build with MLA_TC_PROFILE=1) and reported by MLA_TC_TRACE.
+#ifdef MLA_TC_PROFILE
+#define MLA_TW(slot, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); \
+    wacc[slot] += clock64() - _t0; return _r; }())
+#define MLA_PROF(stmt) stmt
+#else
+#define MLA_TW(slot, expr) (expr)
+#define MLA_PROF(stmt)
+#endif
 
 struct TileIter {
     int64_t g, j, tiles, keys;
@@ -160,14 +184,14 @@ __device__ __forceinline__ void advance(const Params& p, TileIter& it) {
 }
 
 struct Bars {
-    uint64_t full[6];       // tile data landed (TMA) - slots (16-bit) or stages (fp32)
-    uint64_t stg_empty[3];  // fp32 staging consumed by the converters
-    uint64_t bf_full[6];    // fp32: converted slot ready
-    uint64_t bf_empty[6];   // slot released by the P.V MMA
-    uint64_t s_full[2];
-    uint64_t p_full[2];
-    uint64_t o_done[2];
-    uint64_t x_full[2];     // peer's partial scores arrived
+    uint64_t full[6];         // TMA data landed: slots (16-bit) or staging buffers (fp32)
+    uint64_t stg_empty[6];    // fp32: staging buffer read by all converter threads
+    uint64_t bf_full[6];      // fp32: converted slot ready
+    uint64_t bf_empty[6];     // slot released by the P.V MMA
+    uint64_t s_full[kSBufs];
+    uint64_t p_full[kSBufs];
+    uint64_t o_done[kSBufs];
+    uint64_t x_full[kXBufs];  // peer's partial scores arrived (st.async byte count)
     uint64_t q_ready;
     uint32_t tmem_base;
     int abort;
@@ -183,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     unsigned char* slots = smem;
     unsigned char* stg = slots + Tr::kSlots * kSlotBytes;
     float* xbuf = reinterpret_cast<float*>(stg + Tr::kStages * kStgBytes);
-    Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<unsigned char*>(xbuf) + 2 * kXBytes);
+    Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<unsigned char*>(xbuf) + kXBufs * kXBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -192,21 +216,24 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     const int64_t cl = cluster_id_x();
     const int64_t t_begin = cl * p.tiles_per_cluster;
     const int64_t t_end = min(t_begin + p.tiles_per_cluster, p.total_tiles);
+    const int64_t n = t_end > t_begin ? t_end - t_begin : 0;   // tiles of this cluster
     volatile int* abort = &bars->abort;
+    MLA_PROF(long long wacc[16] = {0};)
+    MLA_PROF(const long long t_kernel0 = clock64();)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 6; ++i) {
             mbar_init(&bars->full[i], 1);
+            mbar_init(&bars->stg_empty[i], 128);
             mbar_init(&bars->bf_full[i], 128);
             mbar_init(&bars->bf_empty[i], 1);
         }
-        for (int i = 0; i < 3; ++i) mbar_init(&bars->stg_empty[i], 128);
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kSBufs; ++i) {
             mbar_init(&bars->s_full[i], 1);
             mbar_init(&bars->p_full[i], 128);
             mbar_init(&bars->o_done[i], 1);
-            mbar_init(&bars->x_full[i], 128);
         }
+        for (int i = 0; i < kXBufs; ++i) mbar_init(&bars->x_full[i], 1);
         mbar_init(&bars->q_ready, 128);
         bars->abort = 0;
         fence_mbar_init();
@@ -222,26 +249,34 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     cluster_sync();   // the peer's barriers exist before any remote arrive
     const uint32_t tmem = bars->tmem_base;
 
-    if (t_begin < t_end) {
+    if (n > 0) {
         if (warp == 0 && lane == 0) {
             // ------------------------------------------------------------ TMA producer
             TileIter it = locate(p, t_begin);
             const uint32_t bytes = uint32_t(NK) * dims * sizeof(T);
-            for (int64_t i = 0; t_begin + i < t_end; ++i, advance(p, it)) {
+            for (int64_t i = 0; i < n; ++i, advance(p, it)) {
                 const int32_t row = int32_t((it.g / p.sq) * p.sk + it.j * NK);
                 trace_put(p, 0, i * 16 + 1);
                 if constexpr (Tr::kConvert) {
-                    const int st = int(i % Tr::kStages);
-                    if (!mbar_wait(&bars->stg_empty[st], uint32_t(((i / Tr::kStages) & 1) ^ 1), abort, p.err,
-                                   ERR_TIMEOUT_BASE + 1)) break;
-                    unsigned char* dst = stg + st * kStgBytes;
-                    mbar_arrive_expect_tx(&bars->full[st], bytes);
-                    tma_load_2d(dst, &tm_ckv, &bars->full[st], int32_t(rank * kHalf), row);
-                    if (rank == 1) tma_load_2d(dst + NK * kHalf * 4, &tm_pe, &bars->full[st], 0, row);
+                    bool okp = true;
+                    for (int h = 0; h < 2 && okp; ++h) {
+                        const int64_t k = 2 * i + h;
+                        const int st = int(k % Tr::kStages);
+                        okp = MLA_TW(0, mbar_wait(&bars->stg_empty[st], uint32_t(((k / Tr::kStages) & 1) ^ 1), abort,
+                                                  p.err, ERR_TIMEOUT_BASE + 1));
+                        if (!okp) break;
+                        unsigned char* dst = stg + st * kStgBytes;
+                        mbar_arrive_expect_tx(&bars->full[st], bytes / 2);
+                        tma_load_2d(dst, &tm_ckv, &bars->full[st], int32_t(rank * kHalf), row + h * kStgRows);
+                        if (rank == 1)
+                            tma_load_2d(dst + kStgRows * kHalf * 4, &tm_pe, &bars->full[st], 0, row + h * kStgRows);
+                    }
+                    if (!okp) break;
                 } else {
                     const int sl = int(i % Tr::kSlots);
-                    if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                                   ERR_TIMEOUT_BASE + 2)) break;
+                    if (!MLA_TW(1, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                                             ERR_TIMEOUT_BASE + 2)))
+                        break;
                     unsigned char* dst = slots + sl * kSlotBytes;
                     mbar_arrive_expect_tx(&bars->full[sl], bytes);
                     for (int c = 0; c < 4; ++c)
@@ -251,6 +286,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             }
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
+            // Order: S(j) then P.V of tile j-2. P.V trails by two tiles (also across
+            // segment boundaries), so the score MMA of the tile the softmax is
+            // preparing never queues behind a P.V on the tensor pipe.
             if (lane == 0) {
                 constexpr uint32_t idesc_s = instr_desc(Tr::kFmt, 128, NK, 0, 0);
                 constexpr uint32_t idesc_o = instr_desc(Tr::kFmt, 128, kHalf, 0, 1);
@@ -258,9 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 TileIter it = locate(p, t_begin);
                 int64_t seg = 0;
                 bool ok = true;
+                bool first_ring[kSBufs] = {true, true, true};
                 auto issue_pv = [&](int64_t i, bool first) -> bool {
-                    const int sb = int(i & 1);
-                    if (!mbar_wait(&bars->p_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3))
+                    const int sb = int(i % kSBufs);
+                    if (!MLA_TW(2, mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
+                                             ERR_TIMEOUT_BASE + 3)))
                         return false;
                     tc_fence_after();
                     const int sl = int(i % Tr::kSlots);
@@ -276,20 +316,21 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     mma_commit(&bars->o_done[sb]);
                     return true;
                 };
-                for (int64_t i = 0; t_begin + i < t_end && ok; ++i) {
+                for (int64_t i = 0; i < n && ok; ++i) {
                     const bool first = (i == 0) || it.j == 0;
-                    const bool last = (t_begin + i + 1 == t_end) || (it.j + 1 == it.tiles);
                     if (first) {
-                        if (!mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)) break;
+                        if (!MLA_TW(3, mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)))
+                            break;
                         ++seg;
                     }
                     const int sl = int(i % Tr::kSlots);
                     trace_put(p, 1, i * 16 + 1);
                     uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
-                    if (!mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)) break;
+                    if (!MLA_TW(4, mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)))
+                        break;
                     tc_fence_after();
                     const uint32_t base = smem_slots + sl * kSlotBytes;
-                    const int sb = int(i & 1);
+                    const int sb = int(i % kSBufs);
                     for (int k = 0; k < dims / 16; ++k) {
                         // B = K [32 keys x 16 dims], K-major, 128B swizzle: chunk k/4, +32 B per k-step.
                         const uint64_t bd = smem_desc(base + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024, 2);
@@ -297,98 +338,135 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     }
                     mma_commit(&bars->s_full[sb]);
                     trace_put(p, 1, i * 16 + 2);
-                    if (!first) ok = issue_pv(i - 1, /*first=*/(i - 1 == 0) || it.j == 1);
-                    if (ok && last) ok = issue_pv(i, first);
+                    first_ring[i % kSBufs] = first;
+                    if (i >= 2) ok = issue_pv(i - 2, first_ring[(i - 2) % kSBufs]);
                     advance(p, it);
                 }
+                for (int64_t i = (n >= 2 ? n - 2 : 0); ok && i < n; ++i) ok = issue_pv(i, first_ring[i % kSBufs]);
             }
         } else if (warp >= 4 && warp < 8) {
             // ------------------------------------------------------------ softmax
+            // Pipelined one tile ahead: iteration i first "prepares" tile i+1 (loads
+            // the next segment's query if one starts, waits for its partial scores,
+            // pushes them to the peer) and then finishes tile i (adds the peer's
+            // partial, online softmax, P to TMEM, epilogue), so the DSMEM round trip
+            // of tile i+1 overlaps the softmax of tile i.
+            // Exchange buffers: the peer can be at most three pushes ahead of my
+            // reads (its push of tile k+1 follows its softmax of k-1, which needed my
+            // push of k-1, made after my softmax of k-3), so four buffers need no
+            // further flow control.
             const int row = threadIdx.x - 128;               // head
             const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
             const float c = p.c_log2;
             const float tau = 8.0f / c;                      // lazy rescale threshold (raw units)
-            float* xrow[2] = {xbuf + row * kXStride, xbuf + kHeads * kXStride + row * kXStride};
-            const uint32_t xpeer[2] = {map_peer(xrow[0], peer), map_peer(xrow[1], peer)};
-            TileIter it = locate(p, t_begin);
+            const uint32_t sw = uint32_t(row & 7);            // chunk swizzle of my exchange row
+            // peer addresses of my exchange row and of the exchange barriers (buffer 0;
+            // the mapping is linear: buffer b is at +b*kXBytes / +b*8)
+            const uint32_t xpeer0 = map_peer(xbuf + row * NK, peer);
+            const uint32_t xbar_peer0 = map_peer(&bars->x_full[0], peer);
             int64_t seg_local = 0;
             float m_run = -INFINITY, l_run = 0.f;
-            for (int64_t i = 0; t_begin + i < t_end; ++i, advance(p, it)) {
-                const bool first = (i == 0) || it.j == 0;
-                const bool last = (t_begin + i + 1 == t_end) || (it.j + 1 == it.tiles);
-                const int sb = int(i & 1);
+            bool ok = true;
+
+            // prepare tile i (iterator itp): my partial scores of tile i are returned in sr
+            auto prepare = [&](int64_t i, const TileIter& itp, uint32_t (&sr)[32]) -> bool {
+                const bool first = (i == 0) || itp.j == 0;
+                const int sb = int(i % kSBufs);
                 if (first) {
+                    // query slice of this group into TMEM as bf16/fp16 pairs: 16-byte
+                    // loads, 64 dims (32 TMEM columns) per chunk, all loads of a chunk
+                    // issued before any conversion
                     __syncwarp();   // tcgen05.st below is warp-collective
-                    // load this group's query slice into TMEM as bf16/fp16 pairs
-                    const int64_t grow = it.g * kHeads + row;
+                    const int64_t grow = itp.g * kHeads + row;
                     const T* qa = static_cast<const T*>(p.qa) + grow * kRank + rank * kHalf;
-                    for (int c32 = 0; c32 < kHalf / 64; ++c32) {
+                    const T* qr = static_cast<const T*>(p.qr) + grow * kRope;
+                    constexpr int kV = 16 / sizeof(T);           // elements per 16-byte vector
+                    const int nchunks = rank == 1 ? 5 : 4;
+                    for (int c32 = 0; c32 < nchunks; ++c32) {
+                        const T* srcp = c32 < 4 ? qa + c32 * 64 : qr;
+                        uint4 v[64 / kV];
+#pragma unroll
+                        for (int q = 0; q < 64 / kV; ++q) v[q] = __ldg(reinterpret_cast<const uint4*>(srcp) + q);
                         uint32_t r[32];
-                        for (int e = 0; e < 32; ++e) {
-                            const float lo = cvt<float>(qa[c32 * 64 + 2 * e]);
-                            const float hi = cvt<float>(qa[c32 * 64 + 2 * e + 1]);
-                            if constexpr (Tr::kFmt == 0) {
-                                __half2 h2 = __floats2half2_rn(lo, hi);
-                                r[e] = *reinterpret_cast<uint32_t*>(&h2);
-                            } else {
-                                r[e] = pack_bf16(lo, hi);
+#pragma unroll
+                        for (int q = 0; q < 64 / kV; ++q) {
+                            if constexpr (sizeof(T) == 4) {
+                                r[2 * q] = pack_bf16(__uint_as_float(v[q].x), __uint_as_float(v[q].y));
+                                r[2 * q + 1] = pack_bf16(__uint_as_float(v[q].z), __uint_as_float(v[q].w));
+                            } else {                                 // 16-bit storage: already pairs
+                                r[4 * q] = v[q].x; r[4 * q + 1] = v[q].y; r[4 * q + 2] = v[q].z; r[4 * q + 3] = v[q].w;
                             }
                         }
                         tmem_st32(tmem + lane_off + kTmemQ + c32 * 32, r);
                     }
-                    if (rank == 1) {
-                        const T* qr = static_cast<const T*>(p.qr) + grow * kRope;
-                        uint32_t r[32];
-                        for (int e = 0; e < 32; ++e) {
-                            const float lo = cvt<float>(qr[2 * e]), hi = cvt<float>(qr[2 * e + 1]);
-                            if constexpr (Tr::kFmt == 0) {
-                                __half2 h2 = __floats2half2_rn(lo, hi);
-                                r[e] = *reinterpret_cast<uint32_t*>(&h2);
-                            } else {
-                                r[e] = pack_bf16(lo, hi);
-                            }
-                        }
-                        tmem_st32(tmem + lane_off + kTmemQ + 128, r);
-                    }
                     tmem_st_wait();
                     tc_fence_before();
                     mbar_arrive(&bars->q_ready);
+                }
+                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 1);
+                // every lane polls, then the warp reconverges: tcgen05.ld is warp-collective
+                if (!__all_sync(0xffffffffu, MLA_TW(5, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort,
+                                                                 p.err, ERR_TIMEOUT_BASE + 6))))
+                    return false;
+                tc_fence_after();
+                MLA_PROF(const long long tph = clock64();)
+                tmem_ld32(tmem + lane_off + kTmemS + sb * NK, sr);
+                tmem_ld_wait();
+                const int xb = int(i % kXBufs);
+                // one thread announces the bytes the peer will push for tile i; then
+                // st.async pushes my partial, counted on the peer's barrier
+                if (row == 0) mbar_arrive_expect_tx(&bars->x_full[xb], uint32_t(kHeads * NK * 4));
+                for (int e = 0; e < NK / 4; ++e)
+                    st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + ((uint32_t(e) ^ sw) << 4), __uint_as_float(sr[4 * e]),
+                                __uint_as_float(sr[4 * e + 1]), __uint_as_float(sr[4 * e + 2]),
+                                __uint_as_float(sr[4 * e + 3]), xbar_peer0 + uint32_t(xb) * 8u);
+                MLA_PROF(wacc[11] += clock64() - tph;)
+                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 3);
+                return true;
+            };
+
+            TileIter it = locate(p, t_begin);     // tile being finished
+            TileIter itn = it;                     // tile being prepared
+            uint32_t sr_cur[32], sr_next[32];
+            MLA_PROF(const long long t_loop0 = clock64();)
+            ok = prepare(0, itn, sr_cur);
+            for (int64_t i = 0; i < n && ok; ++i) {
+                const bool first = (i == 0) || it.j == 0;
+                const bool last = (i + 1 == n) || (it.j + 1 == it.tiles);
+                const int sb = int(i % kSBufs);
+                if (i + 1 < n) {
+                    advance(p, itn);
+                    if (!prepare(i + 1, itn, sr_next)) break;
+                }
+                if (first) {
                     m_run = -INFINITY;
                     l_run = 0.f;
                 }
-                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 1);
-                // every lane polls, then the warp reconverges: the tcgen05.ld below is warp-collective
-                if (!__all_sync(0xffffffffu,
-                                mbar_wait(&bars->s_full[sb], uint32_t((i >> 1) & 1), abort, p.err, ERR_TIMEOUT_BASE + 6)))
+                const int xb = int(i % kXBufs);
+                if (!__all_sync(0xffffffffu, MLA_TW(6, mbar_wait(&bars->x_full[xb], uint32_t((i / kXBufs) & 1), abort,
+                                                                 p.err, ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true))))
                     break;
-                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 2);
-                tc_fence_after();
-                uint32_t sr[32];
-                tmem_ld32(tmem + lane_off + kTmemS + sb * NK, sr);
-                tmem_ld_wait();
-                // send my partial scores to the peer, receive its partial
-                for (int e = 0; e < NK; e += 4)
-                    st_cluster_v4(xpeer[sb] + e * 4, __uint_as_float(sr[e]), __uint_as_float(sr[e + 1]),
-                                  __uint_as_float(sr[e + 2]), __uint_as_float(sr[e + 3]));
-                mbar_arrive_remote(&bars->x_full[sb], peer);
-                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 3);
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_full[sb], uint32_t((i >> 1) & 1), abort, p.err,
-                                                       ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true)))
-                    break;
+                MLA_PROF(const long long tph = clock64();)
                 float s[NK];
                 const int64_t key0 = it.j * NK;
+                const float* xr = xbuf + xb * (kHeads * NK) + row * NK;
+#pragma unroll
+                for (int e = 0; e < NK / 4; ++e) {
+                    const float4 pv = *reinterpret_cast<const float4*>(xr + ((e ^ int(sw)) << 2));
+                    s[4 * e] = __uint_as_float(sr_cur[4 * e]) + pv.x;
+                    s[4 * e + 1] = __uint_as_float(sr_cur[4 * e + 1]) + pv.y;
+                    s[4 * e + 2] = __uint_as_float(sr_cur[4 * e + 2]) + pv.z;
+                    s[4 * e + 3] = __uint_as_float(sr_cur[4 * e + 3]) + pv.w;
+                }
+                if (key0 + NK > it.keys) {            // ragged last tile of a group (warp-uniform)
+                    const int valid = int(it.keys - key0);
+#pragma unroll
+                    for (int e = 0; e < NK; ++e)
+                        if (e >= valid) s[e] = -INFINITY;
+                }
                 float mt = -INFINITY;
-                for (int e = 0; e < NK; e += 4) {
-                    const float4 pv = *reinterpret_cast<const float4*>(xrow[sb] + e);
-                    s[e] = __uint_as_float(sr[e]) + pv.x;
-                    s[e + 1] = __uint_as_float(sr[e + 1]) + pv.y;
-                    s[e + 2] = __uint_as_float(sr[e + 2]) + pv.z;
-                    s[e + 3] = __uint_as_float(sr[e + 3]) + pv.w;
-                }
-                for (int e = 0; e < NK; ++e) {
-                    if (key0 + e >= it.keys) s[e] = -INFINITY;
-                    mt = fmaxf(mt, s[e]);
-                }
+#pragma unroll
+                for (int e = 0; e < NK; ++e) mt = fmaxf(mt, s[e]);
                 if (first) {
                     m_run = mt;
                 } else if (__any_sync(0xffffffffu, mt > m_run + tau)) {
@@ -396,9 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     // below are warp-collective. Every lane of the warp moves to its own
                     // new maximum (alpha <= 1). The peer CTA sees the same scores, so it
                     // takes the same decision. Waits for P.V of the previous tile first.
-                    const int pb = int((i - 1) & 1);
-                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) >> 1) & 1), abort,
-                                                           p.err, ERR_TIMEOUT_BASE + 8)))
+                    const int pb = int((i - 1) % kSBufs);
+                    if (!__all_sync(0xffffffffu, MLA_TW(7, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) / kSBufs) & 1),
+                                                                     abort, p.err, ERR_TIMEOUT_BASE + 8))))
                         break;
                     tc_fence_after();
                     mt = fmaxf(mt, m_run);
@@ -417,6 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 const float mc = m_run * c;
                 uint32_t pk[NK / 2];
                 float ls = 0.f;
+#pragma unroll
                 for (int e = 0; e < NK; e += 2) {
                     const float p0 = ex2(fmaf(s[e], c, -mc));
                     const float p1 = ex2(fmaf(s[e + 1], c, -mc));
@@ -434,10 +513,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
+                MLA_PROF(wacc[12] += clock64() - tph;)
                 if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 4);
                 if (last) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[sb], uint32_t((i >> 1) & 1), abort, p.err,
-                                                           ERR_TIMEOUT_BASE + 9)))
+                    MLA_PROF(const long long tep = clock64();)
+                    if (!__all_sync(0xffffffffu, MLA_TW(8, mbar_wait(&bars->o_done[sb], uint32_t((i / kSBufs) & 1), abort,
+                                                                     p.err, ERR_TIMEOUT_BASE + 9))))
                         break;
                     tc_fence_after();
                     const int64_t slot = cl * p.max_segs + seg_local;
@@ -457,51 +538,96 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     }
                     tc_fence_before();
                     ++seg_local;
+                    MLA_PROF(wacc[13] += clock64() - tep;)
                 }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) sr_cur[e] = sr_next[e];
+                advance(p, it);
             }
-        } else if (warp >= 8 && Tr::kConvert) {
+            MLA_PROF(wacc[14] = clock64() - t_loop0;)
+        } else if ((warp == 2 || warp == 3 || warp >= 8) && Tr::kConvert) {
             // ------------------------------------------------------------ fp32 -> bf16
-            const int ct = threadIdx.x - 256;
-            for (int64_t i = 0; t_begin + i < t_end; ++i) {
-                const int st = int(i % Tr::kStages), sl = int(i % Tr::kSlots);
-                if (!mbar_wait(&bars->full[st], uint32_t((i / Tr::kStages) & 1), abort, p.err, ERR_TIMEOUT_BASE + 10))
+            // Converts two fp32 half-tile staging buffers into one bf16 128B-swizzled
+            // slot. Every thread reads its share of a half tile into registers and
+            // releases the staging buffer before writing, so the next TMA load can
+            // start at once.
+            const int ct = (warp < 4 ? (warp - 2) : (warp - 6)) * 32 + lane;
+            constexpr int kU = kStgRows * 32 / 128;   // c_kv units of 8 floats per thread per half tile
+            constexpr int kP = kStgRows * 8 / 128;    // pe units per thread per half tile (CTA 1)
+            static_assert(kU * 128 == kStgRows * 32 && kP * 128 == kStgRows * 8, "converter mapping");
+            bool okc = true;
+            for (int64_t i = 0; okc && i < n; ++i) {
+                const int sl = int(i % Tr::kSlots);
+                if (!MLA_TW(10, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                                          ERR_TIMEOUT_BASE + 11)))
                     break;
-                if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                               ERR_TIMEOUT_BASE + 11)) break;
                 if (ct == 0) trace_put(p, 3, i * 16 + 2);
-                const float* src = reinterpret_cast<const float*>(stg + st * kStgBytes);
-                unsigned char* dst = slots + sl * kSlotBytes;
-                // c_kv half: NK rows x 256 floats = NK*32 units of 8 floats
-                for (int u = ct; u < NK * 32; u += 128) {
-                    const int r = u >> 5, c8 = u & 31;
-                    const float4 a = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8);
-                    const float4 b = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8 + 4);
-                    uint4 v;
-                    v.x = pack_bf16(a.x, a.y); v.y = pack_bf16(a.z, a.w);
-                    v.z = pack_bf16(b.x, b.y); v.w = pack_bf16(b.z, b.w);
-                    const int chunk = c8 >> 3, unit = (c8 & 7) ^ (r & 7);
-                    *reinterpret_cast<uint4*>(dst + chunk * kChunkBytes + r * 128 + unit * 16) = v;
-                }
-                if (rank == 1) {
-                    const float* pe = src + NK * kHalf;
-                    for (int u = ct; u < NK * 8; u += 128) {
-                        const int r = u >> 3, c8 = u & 7;
-                        const float4 a = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8);
-                        const float4 b = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8 + 4);
-                        uint4 v;
-                        v.x = pack_bf16(a.x, a.y); v.y = pack_bf16(a.z, a.w);
-                        v.z = pack_bf16(b.x, b.y); v.w = pack_bf16(b.z, b.w);
-                        const int unit = c8 ^ (r & 7);
-                        *reinterpret_cast<uint4*>(dst + 4 * kChunkBytes + r * 128 + unit * 16) = v;
+                unsigned char* buf = slots + sl * kSlotBytes;
+                for (int h = 0; h < 2; ++h) {
+                    const int64_t k = 2 * i + h;
+                    const int st = int(k % Tr::kStages);
+                    if (!MLA_TW(9, mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
+                                             ERR_TIMEOUT_BASE + 10))) {
+                        okc = false;
+                        break;
+                    }
+                    const float* src = reinterpret_cast<const float*>(stg + st * kStgBytes);
+                    uint4 cv[kU], pv[kP];
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        const int u = ct + q * 128, r = u >> 5, c8 = u & 31;
+                        const float4 a = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8);
+                        const float4 b = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8 + 4);
+                        cv[q] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
+                                           pack_bf16(b.z, b.w));
+                    }
+                    if (rank == 1) {
+                        const float* pe = src + kStgRows * kHalf;
+#pragma unroll
+                        for (int q = 0; q < kP; ++q) {
+                            const int u = ct + q * 128, r = u >> 3, c8 = u & 7;
+                            const float4 a = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8);
+                            const float4 b = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8 + 4);
+                            pv[q] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
+                                               pack_bf16(b.z, b.w));
+                        }
+                    }
+                    // my generic-proxy reads of the staging buffer must be ordered before
+                    // the next TMA (async-proxy) write into it
+                    fence_proxy_async_smem();
+                    mbar_arrive(&bars->stg_empty[st]);
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        const int u = ct + q * 128, r = h * kStgRows + (u >> 5), c8 = u & 31;
+                        const int chunk = c8 >> 3, unit = (c8 & 7) ^ (r & 7);
+                        *reinterpret_cast<uint4*>(buf + chunk * kChunkBytes + r * 128 + unit * 16) = cv[q];
+                    }
+                    if (rank == 1) {
+#pragma unroll
+                        for (int q = 0; q < kP; ++q) {
+                            const int u = ct + q * 128, r = h * kStgRows + (u >> 3), c8 = u & 7;
+                            const int unit = c8 ^ (r & 7);
+                            *reinterpret_cast<uint4*>(buf + 4 * kChunkBytes + r * 128 + unit * 16) = pv[q];
+                        }
                     }
                 }
+                if (!okc) break;
                 fence_proxy_async_smem();
                 mbar_arrive(&bars->bf_full[sl]);
-                mbar_arrive(&bars->stg_empty[st]);
             }
         }
     }
 
+#ifdef MLA_TC_PROFILE
+    if (p.trace) {
+        const bool rep = (warp == 0 && lane == 0) || (warp == 1 && lane == 0) || (warp == 4 && lane == 0) ||
+                         (warp == 2 && lane == 0);
+        if (rep)
+            for (int k = 0; k < 15; ++k)
+                if (wacc[k]) trace_put(p, 8 + k, wacc[k] / 1000);
+        if (threadIdx.x == 0) trace_put(p, 23, (clock64() - t_kernel0) / 1000);
+    }
+#endif
     if (threadIdx.x == 0) trace_put(p, 4, 1);
     tc_fence_before();
     __syncthreads();
@@ -517,6 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     __syncwarp();
     cluster_sync();
     if (threadIdx.x == 0) trace_put(p, 6, 1);
+    if (p.trace) __threadfence_system();
 }
 
 // Combine the segments of every (group, head) row into a normalised context.
@@ -572,7 +699,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <typename T>
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint32_t box_cols, bool swz) {
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint32_t box_cols, uint32_t box_rows,
+              bool swz) {
     auto fn = encode_fn();
     if (!fn) return false;
     const CUtensorMapDataType dt = std::is_same<T, float>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -580,7 +708,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint
                                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
     cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
     cuuint64_t strides[1] = {cuuint64_t(cols) * sizeof(T)};
-    cuuint32_t box[2] = {box_cols, cuuint32_t(NK)};
+    cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -666,8 +794,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         CUtensorMap tm_ckv, tm_pe;
         const bool swz = !Traits<T>::kConvert;
         const int64_t rows = a.batch * a.sk;
-        if (!make_map<T>(&tm_ckv, a.c_kv, rows, kRank, swz ? 64 : kHalf, swz) ||
-            !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, 64, swz))
+        const uint32_t box_rows = swz ? uint32_t(NK) : uint32_t(kStgRows);
+        if (!make_map<T>(&tm_ckv, a.c_kv, rows, kRank, swz ? 64 : kHalf, box_rows, swz) ||
+            !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, 64, box_rows, swz))
             return set_error(MLA_ERR_CUDA, "MLA: cuTensorMapEncodeTiled failed (alignment of c_kv / pe_cache?)");
 
         if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess)
@@ -689,9 +818,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         cfg.numAttrs = 1;
         int* trace_host = nullptr;
         if (getenv("MLA_TC_TRACE")) {   // debug: progress words polled from the host while the kernel runs
-            if (cudaHostAlloc(reinterpret_cast<void**>(&trace_host), 2 * 148 * 8 * sizeof(int), cudaHostAllocMapped) ==
+            if (cudaHostAlloc(reinterpret_cast<void**>(&trace_host), 2 * 148 * 32 * sizeof(int), cudaHostAllocMapped) ==
                 cudaSuccess) {
-                memset(trace_host, 0xff, 2 * 148 * 8 * sizeof(int));
+                memset(trace_host, 0xff, 2 * 148 * 32 * sizeof(int));
                 cudaHostGetDevicePointer(reinterpret_cast<void**>(&p.trace), trace_host, 0);
             }
         }
@@ -709,9 +838,12 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             fprintf(stderr, "[mla trace] kernel %s; grid %lld CTAs\n", done ? "finished" : "STILL RUNNING after 5 s",
                     (long long)(2 * pl.nclusters));
             for (int64_t b = 0; b < 2 * pl.nclusters && b < 296; ++b) {
-                const volatile int* t = trace_host + b * 8;
-                fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d\n", (long long)b,
-                        t[0], t[1], t[2], t[3], t[4], t[5], t[6]);
+                const volatile int* t = trace_host + b * 32;
+                fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d | kcyc total %d "
+                        "stg_empty %d bf_empty(p) %d p_full %d q_ready %d bf_full %d s_full %d x_full %d o_resc %d "
+                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d\n",
+                        (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[23], t[8], t[9], t[10], t[11], t[12],
+                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22]);
             }
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);
