@@ -129,7 +129,11 @@ mla_status_t mla_q_absorbed_workspace_size(mla_dtype_t dtype, mla_precision_t pr
     QArgs a{};
     a.batch = batch; a.sq = sq; a.hidden = hidden; a.q_lora = q_lora;
     a.heads = heads; a.nope = nope; a.rope = rope; a.kv_rank = kv_rank;
-    *bytes = dispatch(dtype, [&](auto t) { return qprep_exact_workspace<decltype(t)>(a); });
+    *bytes = dispatch(dtype, [&](auto t) {
+        using T = decltype(t);
+        return (precision == MLA_PREC_TENSOR && qprep_tensor_supported<T>(a)) ? qprep_tensor_workspace<T>(a)
+                                                                               : qprep_exact_workspace<T>(a);
+    });
     return MLA_OK;
 }
 
@@ -144,11 +148,17 @@ mla_status_t mla_q_absorbed(mla_dtype_t dtype, mla_precision_t precision, const 
         return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA q_absorbed: null operand pointer");
     QArgs a{x, W_q_a, q_norm_w, W_q_b, W_uk, positions, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank,
             eps, q_absorbed, q_rope, workspace, workspace_bytes};
-    const size_t need = dispatch(dtype, [&](auto t) { return qprep_exact_workspace<decltype(t)>(a); });
+    const bool tc = dispatch(dtype, [&](auto t) {
+        return precision == MLA_PREC_TENSOR && qprep_tensor_supported<decltype(t)>(a);
+    });
+    const size_t need = dispatch(dtype, [&](auto t) {
+        return tc ? qprep_tensor_workspace<decltype(t)>(a) : qprep_exact_workspace<decltype(t)>(a);
+    });
     if (need > 0 && (!workspace || workspace_bytes < need))
         return set_error(MLA_ERR_WORKSPACE, "MLA q_absorbed: workspace of %zu bytes needed, %zu given", need,
                          workspace ? workspace_bytes : size_t(0));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (tc) return dispatch(dtype, [&](auto t) { return qprep_tensor<decltype(t)>(a, st); });
     return dispatch(dtype, [&](auto t) { return qprep_exact<decltype(t)>(a, st); });
 }
 

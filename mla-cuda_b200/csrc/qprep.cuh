@@ -29,6 +29,10 @@ struct AArgs {
 template <typename T> size_t qprep_exact_workspace(const QArgs& a);
 template <typename T> mla_status_t qprep_exact(const QArgs& a, cudaStream_t st);
 
+template <typename T> bool qprep_tensor_supported(const QArgs& a);
+template <typename T> size_t qprep_tensor_workspace(const QArgs& a);
+template <typename T> mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st);
+
 template <typename T> size_t attn_exact_workspace(const AArgs& a);
 template <typename T> mla_status_t attn_exact(const AArgs& a, cudaStream_t st);
 

@@ -13,8 +13,10 @@
 // result is deterministic run to run.
 #include "qprep.cuh"
 #include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
 
 #include <cmath>
+#include <type_traits>
 
 namespace mla {
 namespace {
@@ -322,5 +324,146 @@ template mla_status_t qprep_exact<float>(const QArgs&, cudaStream_t);
 template mla_status_t qprep_exact<double>(const QArgs&, cudaStream_t);
 template mla_status_t qprep_exact<__half>(const QArgs&, cudaStream_t);
 template mla_status_t qprep_exact<__nv_bfloat16>(const QArgs&, cudaStream_t);
+
+// ------------------------------------------------------------ tensor-core Q-prep
+// MLA_PREC_TENSOR: 2a1 and 2a2 run as split-K tcgen05 GEMMs (kind::tf32 for
+// fp32 storage, kind::f16 for 16-bit) writing fp32 partials that the same
+// RMSNorm and RoPE kernels reduce; 2c is a per-head tcgen05 GEMM for fp32
+// storage (its fp32 left operand needs fp32 weights) and the CUDA-core kernel
+// otherwise.
+namespace {
+
+struct QTPlan {
+    int split1, split2;
+    int64_t chunk1, chunk2;
+    size_t off_err, off_p1, off_qlat, off_p2, off_qnope, total;
+};
+
+int tc_split(int64_t tiles, int64_t K, int64_t bk, int waves, int64_t& chunk) {
+    const int64_t want = int64_t(waves) * sm_count();
+    int64_t s = want / (tiles > 0 ? tiles : 1);
+    const int64_t kblocks = ceil_div(K, bk);
+    if (s > kblocks / 4) s = kblocks / 4;     // at least four K blocks per slice
+    if (s < 1) s = 1;
+    const int64_t cb = ceil_div(kblocks, s);
+    chunk = cb * bk;
+    return int(ceil_div(kblocks, cb));
+}
+
+template <typename T>
+QTPlan make_tplan(const QArgs& a) {
+    using Acc = acc_t<T>;
+    QTPlan p{};
+    const int64_t M = a.batch * a.sq;
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    const int64_t bk = tc_gemm_bk<T>();
+    const int64_t mt = ceil_div(M, 128);
+    p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), a.hidden, bk, 1, p.chunk1);
+    p.split2 = tc_split(mt * ceil_div(ncols, 256), a.q_lora, bk, 2, p.chunk2);
+    size_t off = 0;
+    p.off_err = off;   off = align_up(off + 256, 256);
+    p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(Acc), 256);
+    p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(T), 256);
+    p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(Acc), 256);
+    p.off_qnope = off; off = align_up(off + size_t(M) * a.heads * a.nope * sizeof(Acc), 256);
+    p.total = off;
+    return p;
+}
+
+}  // namespace
+
+template <typename T>
+bool qprep_tensor_supported(const QArgs& a) {
+    if constexpr (std::is_same<T, double>::value) return false;
+    else {
+        constexpr int64_t v = 16 / sizeof(T);   // TMA: 16-byte strides
+        const int64_t ncols = a.heads * (a.nope + a.rope);
+        return a.q_lora % 32 == 0 && ncols % 32 == 0 && a.kv_rank % 32 == 0 && a.hidden % v == 0 &&
+               a.q_lora % v == 0 && a.nope % 4 == 0 && a.batch * a.sq > 0;
+    }
+}
+
+template <typename T>
+size_t qprep_tensor_workspace(const QArgs& a) { return make_tplan<T>(a).total; }
+
+template <typename T>
+mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
+    using Acc = acc_t<T>;
+    const QTPlan p = make_tplan<T>(a);
+    const int64_t M = a.batch * a.sq;
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    char* ws = static_cast<char*>(a.workspace);
+    int* err = reinterpret_cast<int*>(ws + p.off_err);
+    Acc* P1 = reinterpret_cast<Acc*>(ws + p.off_p1);
+    T* q_lat = reinterpret_cast<T*>(ws + p.off_qlat);
+    Acc* P2 = reinterpret_cast<Acc*>(ws + p.off_p2);
+    Acc* q_nope = reinterpret_cast<Acc*>(ws + p.off_qnope);
+    if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
+        return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
+
+    TcGemm g1{};   // 2a1: x [M, hidden] @ W_q_a [hidden, q_lora]
+    g1.A = a.x; g1.a_dims[0] = a.hidden; g1.a_dims[1] = 1; g1.a_dims[2] = M; g1.a_ld[0] = a.hidden; g1.a_ld[1] = a.hidden;
+    g1.B = a.W_q_a; g1.b_mn = true; g1.b_dims[0] = a.q_lora; g1.b_dims[1] = a.hidden; g1.b_dims[2] = 1;
+    g1.b_ld[0] = a.q_lora; g1.b_ld[1] = a.q_lora * a.hidden;
+    g1.M = M; g1.N = a.q_lora; g1.K = a.hidden; g1.Z = p.split1; g1.split = true; g1.k_chunk = p.chunk1;
+    g1.C = P1; g1.c_is_t = false; g1.c_ldm = a.q_lora; g1.c_ldz = M * a.q_lora; g1.bn = 128; g1.err = err;
+    MLA_TRY(tc_gemm<T>(g1, st));
+
+    lat_norm_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, p.split1, static_cast<const T*>(a.q_norm_w), q_lat, M,
+                                                     a.q_lora, Acc(a.eps));
+    MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
+
+    TcGemm g2{};   // 2a2: q_lat [M, q_lora] @ W_q_b [q_lora, H*(nope+rope)]
+    g2.A = q_lat; g2.a_dims[0] = a.q_lora; g2.a_dims[1] = 1; g2.a_dims[2] = M; g2.a_ld[0] = a.q_lora; g2.a_ld[1] = a.q_lora;
+    g2.B = a.W_q_b; g2.b_mn = true; g2.b_dims[0] = ncols; g2.b_dims[1] = a.q_lora; g2.b_dims[2] = 1;
+    g2.b_ld[0] = ncols; g2.b_ld[1] = ncols * a.q_lora;
+    g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = p.split2; g2.split = true; g2.k_chunk = p.chunk2;
+    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 256; g2.err = err;
+    MLA_TRY(tc_gemm<T>(g2, st));
+
+    RopeTable<T> tab{};
+    for (int64_t j = 0; j < a.rope / 2; ++j) {
+        const double pw = std::pow(10000.0, double(2 * j) / double(a.rope));
+        tab.inv_freq[j] = Acc(1) / Acc(pw);
+    }
+    {
+        const int64_t total = M * a.heads * (a.nope + a.rope / 2);
+        int64_t blocks = ceil_div(total, 256);
+        const int64_t cap = 16LL * sm_count();
+        if (blocks > cap) blocks = cap;
+        if (blocks < 1) blocks = 1;
+        rope_gather_kernel<T><<<unsigned(blocks), 256, 0, st>>>(P2, p.split2, a.positions, q_nope,
+                                                                 static_cast<T*>(a.q_rope), M, a.sq, a.heads, a.nope,
+                                                                 a.rope, tab);
+        MLA_TRY(check_launch("q rope (2b)"));
+    }
+    if constexpr (std::is_same<T, float>::value) {
+        TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h]
+        g3.A = q_nope; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;
+        g3.a_ld[0] = a.nope; g3.a_ld[1] = a.heads * a.nope;
+        g3.B = a.W_uk; g3.b_mn = true; g3.b_dims[0] = a.kv_rank; g3.b_dims[1] = a.nope; g3.b_dims[2] = a.heads;
+        g3.b_ld[0] = a.kv_rank; g3.b_ld[1] = a.nope * a.kv_rank;
+        g3.M = M; g3.N = a.kv_rank; g3.K = a.nope; g3.Z = int(a.heads); g3.split = false; g3.k_chunk = a.nope;
+        g3.C = a.q_absorbed; g3.c_is_t = true; g3.c_ldm = a.heads * a.kv_rank; g3.c_ldz = a.kv_rank;
+        g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err;
+        return tc_gemm<T>(g3, st);
+    } else {
+        if (M <= 16)
+            return launch_absorb<CfgSmall<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk),
+                                                   static_cast<T*>(a.q_absorbed), a, M, st);
+        return launch_absorb<CfgBig<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk), static_cast<T*>(a.q_absorbed),
+                                             a, M, st);
+    }
+}
+
+#define MLA_QT(T) \
+    template bool qprep_tensor_supported<T>(const QArgs&); \
+    template size_t qprep_tensor_workspace<T>(const QArgs&); \
+    template mla_status_t qprep_tensor<T>(const QArgs&, cudaStream_t);
+MLA_QT(float)
+MLA_QT(double)
+MLA_QT(__half)
+MLA_QT(__nv_bfloat16)
+#undef MLA_QT
 
 }  // namespace mla

@@ -36,6 +36,7 @@
 // (fp32 storage only).
 #include "tc.cuh"
 #include "sm100.cuh"
+#include "tc_gemm.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -648,7 +649,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
 
 // Combine the segments of every (group, head) row into a normalised context.
 // One warp per row; the cluster segments covering group g are contiguous.
-__global__ void __launch_bounds__(256) combine_kernel(const Params p, float* __restrict__ O_norm, int64_t groups)
+template <typename OutT>
+__global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups)
 {
     const int64_t rowid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -680,8 +682,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const Params p, float* __r
         for (int e = 0; e < 16; ++e) acc[e] += w * src[e * 32 + lane];
     }
     const float inv = 1.f / L;
-    float* dst = O_norm + rowid * kRank;
-    for (int e = 0; e < 16; ++e) dst[e * 32 + lane] = acc[e] * inv;
+    OutT* dst = O_norm + rowid * kRank;
+    for (int e = 0; e < 16; ++e) dst[e * 32 + lane] = cvt<OutT>(acc[e] * inv);
 }
 
 // ---------------------------------------------------------------- host side
@@ -849,9 +851,25 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             cudaFreeHost(trace_host);
         }
         const int64_t rows_total = pl.groups * kHeads;
-        combine_kernel<<<unsigned((rows_total * 32 + 255) / 256), 256, 0, st>>>(p, O_norm, pl.groups);
+        const unsigned cblocks = unsigned((rows_total * 32 + 255) / 256);
+        if (a.v_dim % 32 != 0) {   // W_uv projection on CUDA cores from an fp32 context
+            combine_kernel<float><<<cblocks, 256, 0, st>>>(p, O_norm, pl.groups);
+            MLA_TRY(check_launch("segment combine"));
+            return attn_out_normalized<T>(a, O_norm, st);
+        }
+        // context in the storage dtype, then out[:, h] = ctx[:, h] @ W_uv[h]^T on the tensor cores
+        T* ctx = reinterpret_cast<T*>(O_norm);
+        combine_kernel<T><<<cblocks, 256, 0, st>>>(p, ctx, pl.groups);
         MLA_TRY(check_launch("segment combine"));
-        return attn_out_normalized<T>(a, O_norm, st);
+        TcGemm g{};
+        g.A = ctx; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;
+        g.a_ld[0] = kRank; g.a_ld[1] = int64_t(kHeads) * kRank;
+        g.B = a.W_uv; g.b_mn = false; g.b_dims[0] = kRank; g.b_dims[1] = a.v_dim; g.b_dims[2] = kHeads;
+        g.b_ld[0] = kRank; g.b_ld[1] = a.v_dim * kRank;
+        g.M = pl.groups; g.N = a.v_dim; g.K = kRank; g.Z = kHeads; g.split = false; g.k_chunk = kRank;
+        g.C = a.out; g.c_is_t = true; g.c_ldm = int64_t(kHeads) * a.v_dim; g.c_ldz = a.v_dim;
+        g.bn = a.v_dim % 256 == 0 ? 256 : 128; g.err = p.err;
+        return tc_gemm<T>(g, st);
     }
 }
 

@@ -113,3 +113,31 @@ def test_tc_box_scale_bf16_config(mcc):
     ref = mcc.mla_attention_ex(*f32, w.scale, precision="exact")
     assert out.dtype == torch.bfloat16
     assert rel_l2(out.float(), ref) < TOL
+
+
+@pytest.mark.parametrize("B,Sq", [(1, 1), (5, 3), (20, 1), (128, 1), (200, 1)])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_tc_q_absorbed_vs_oracle(mcc, B, Sq, dtype):
+    """Tensor-core Q-prep (tcgen05 projections, tf32 or bf16/fp16 operands)
+    against the fp64 oracle on the same (storage-rounded) inputs."""
+    w = mc.Workload("q", B, Sq, 8, dtype=dtype)
+    t = mc.make_inputs(w, seed=B * 10 + Sq)
+    g = {k: v.to(DEV) for k, v in t.items()}
+    qa, qr = mcc.q_absorbed_ex(g["x"], g["W_q_a"], g["q_norm_w"], g["W_q_b"], g["W_uk"], g["positions"],
+                               mc.NOPE, mc.ROPE, mc.EPS, precision="tensor")
+    assert qa.dtype == dtype and qr.dtype == dtype
+    t64 = {k: (v.double() if v.is_floating_point() else v) for k, v in t.items()}
+    ra, rr = orc.q_absorbed(t64["x"], t64["W_q_a"], t64["q_norm_w"], t64["W_q_b"], t64["W_uk"], t64["positions"])
+    assert rel_l2(qa.cpu(), ra) < TOL
+    assert rel_l2(qr.cpu(), rr) < TOL
+
+
+def test_tc_forward_c0_vs_reference(mcc):
+    """Whole layer forward at config 0, tensor precision, against the reference's fp64 output."""
+    d = load_golden("forward_c0.npz")
+    t = {k: v.to(DEV) for k, v in mc.make_inputs(mc.CONFIGS["c0"], seed=0).items()}
+    qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                               mc.NOPE, mc.ROPE, mc.EPS, precision="tensor")
+    out = mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], mc.SCALE, precision="tensor")
+    assert rel_l2(qa.cpu(), d["qa64_full"]) < TOL
+    assert rel_l2(out.cpu(), d["out64_full"]) < TOL
