@@ -14,6 +14,9 @@
 #include "sm100.cuh"
 #include "tma_host.cuh"
 
+#include <cstdio>
+#include <cstdlib>
+
 namespace mla {
 namespace tcg {
 
@@ -27,6 +30,7 @@ struct Run {
     int Z, split, b_mn, c_is_t;
     void* C; int64_t c_ldm, c_ldz;
     int* err;
+    int dbg;
 };
 
 template <typename T> constexpr uint32_t fmt() {
@@ -109,12 +113,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
             const int s = int(i % S);
             if (!mbar_wait(&full[s], uint32_t((i / S) & 1), abort, r.err, ERR_TIMEOUT_BASE + 2)) { ok = false; break; }
             tc_fence_after();
+            if (r.dbg && i == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+                printf("[gemm dbg] nkb %lld kb %lld A0 %08x %08x B0 %08x %08x\n", (long long)nkb, (long long)kb,
+                       reinterpret_cast<const uint32_t*>(As)[0], reinterpret_cast<const uint32_t*>(As)[1],
+                       reinterpret_cast<const uint32_t*>(Bs)[0], reinterpret_cast<const uint32_t*>(Bs)[1]);
             const uint32_t a0 = smem_u32(As + s * a_bytes<T, BN>());
             const uint32_t b0 = smem_u32(Bs + s * b_bytes<T, BN>());
             for (int kk = 0; kk < BK / kInstK; ++kk) {
                 const uint64_t ad = smem_desc(a0 + kk * 32, 16, 1024, 2);
-                // B MN-major: column groups BK*128 bytes apart (LBO), 8-row K groups 1024 apart (SBO)
-                const uint64_t bd = r.b_mn ? smem_desc(b0 + kk * (kInstK * 128), BK * 128, 1024, 2)
+                // B MN-major: column groups BK*128 bytes apart (LBO), K-row groups SBO apart:
+                // 8 rows / 1024 B with the 16-byte swizzle atoms of 16-bit types; for 32-bit
+                // (tf32) operands the MN-major layout uses 32-byte atoms, 4-row groups (512 B).
+                constexpr bool kA32 = sizeof(T) == 4;
+                const uint64_t bd = r.b_mn ? smem_desc(b0 + kk * (kInstK * 128), BK * 128, kA32 ? 512 : 1024,
+                                                       kA32 ? 1 : 2)
                                            : smem_desc(b0 + kk * 32, 16, 1024, 2);
                 if constexpr (std::is_same<T, float>::value) mma_ss_tf32(tmem, ad, bd, idesc, (i | kk) ? 1u : 0u);
                 else mma_ss(tmem, ad, bd, idesc, (i | kk) ? 1u : 0u);
@@ -142,6 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                     for (int e = 0; e < 32; ++e) v[e] = 0u;
                 }
                 const int64_t n = n0 + c * 32;
+                if (r.dbg && c == 0 && row == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+                    printf("[gemm dbg] acc row0 %f %f  M %lld N %lld ldm %lld\n", __uint_as_float(v[0]),
+                           __uint_as_float(v[1]), (long long)r.M, (long long)r.N, (long long)r.c_ldm);
                 if (m >= r.M || n >= r.N) continue;
                 const int64_t off = m * r.c_ldm + int64_t(z) * r.c_ldz + n;
                 if (!r.c_is_t || std::is_same<T, float>::value) {
@@ -187,10 +202,11 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
     const uint32_t bbox_mn[3] = {uint32_t(BK), uint32_t(BK), 1u};
     const uint32_t bbox_k[3] = {uint32_t(BK), uint32_t(BN), 1u};
     if (!make_map_3d<T>(&ta, g.A, g.a_dims, g.a_ld, abox, true) ||
-        !make_map_3d<T>(&tb, g.B, g.b_dims, g.b_ld, g.b_mn ? bbox_mn : bbox_k, true))
+        !make_map_3d<T>(&tb, g.B, g.b_dims, g.b_ld, g.b_mn ? bbox_mn : bbox_k, true,
+                        /*atom32=*/g.b_mn && sizeof(T) == 4))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.k_chunk, g.Z, g.split ? 1 : 0, g.b_mn ? 1 : 0, g.c_is_t ? 1 : 0, g.C, g.c_ldm, g.c_ldz,
-          g.err};
+          g.err, getenv("MLA_GEMM_DEBUG") ? 1 : 0};
     auto kern = tc_gemm_kernel<T, BN>;
     const size_t smem = smem_bytes<T, BN>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));

@@ -31,10 +31,11 @@ template <typename T> constexpr CUtensorMapDataType tma_dtype() {
 }
 
 // 3-D map: dims innermost first (elements), strides of dims 1 and 2 in elements,
-// box in elements, 128-byte swizzle when `swz`.
+// box in elements, 128-byte swizzle when `swz` (with 32-byte swizzle atoms when
+// `atom32`: the layout the tensor cores want for MN-major 32-bit operands).
 template <typename T>
 inline bool make_map_3d(CUtensorMap* m, const void* base, const int64_t dims[3], const int64_t strides[2],
-                        const uint32_t box[3], bool swz) {
+                        const uint32_t box[3], bool swz, bool atom32 = false) {
     auto fn = tma_encode_fn();
     if (!fn) return false;
     cuuint64_t d[3] = {cuuint64_t(dims[0]), cuuint64_t(dims[1]), cuuint64_t(dims[2])};
@@ -42,7 +43,9 @@ inline bool make_map_3d(CUtensorMap* m, const void* base, const int64_t dims[3],
     cuuint32_t b[3] = {box[0], box[1], box[2]};
     cuuint32_t e[3] = {1, 1, 1};
     return fn(m, tma_dtype<T>(), 3, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              !swz ? CU_TENSOR_MAP_SWIZZLE_NONE
+                   : atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
