@@ -30,10 +30,11 @@
 // storage is converted to bf16 in shared memory after the TMA load, so HBM
 // traffic stays one read of the fp32 cache.
 //
-// Warp roles (320 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
-// owner, warps 4-7 softmax (thread i <-> TMEM lane i <-> head i; a warp reaches
-// only TMEM lanes 32*(warp%4)..+31), warps 2, 3, 8, 9 fp32->bf16 converters
-// (fp32 storage only).
+// Warp roles (256 threads, two warps per SM sub-partition so that each thread
+// may hold up to 255 registers): warp 0 TMA producer, warp 1 MMA issuer and
+// TMEM owner, warps 2-3 fp32->bf16 converters (fp32 storage only), warps 4-7
+// softmax (thread i <-> TMEM lane i <-> head i; a warp reaches only TMEM lanes
+// 32*(warp%4)..+31).
 #include "tc.cuh"
 #include "sm100.cuh"
 #include "tc_gemm.cuh"
@@ -62,7 +63,8 @@ constexpr int kHeads = 128;
 constexpr int kRank = 512;
 constexpr int kRope = 64;
 constexpr int kHalf = 256;                // latent dims per CTA
-constexpr int kThreads = 320;
+constexpr int kThreads = 256;
+constexpr int kConvThreads = 64;         // fp32 -> bf16 converter threads (warps 2, 3)
 constexpr int kChunkBytes = NK * 128;     // one 64-dim chunk of a tile (128-byte rows)
 constexpr int kSlotBytes = 5 * kChunkBytes;
 constexpr int kStgRows = NK / 2;          // an fp32 staging buffer holds half a key tile
@@ -225,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     if (threadIdx.x == 0) {
         for (int i = 0; i < 6; ++i) {
             mbar_init(&bars->full[i], 1);
-            mbar_init(&bars->stg_empty[i], 128);
-            mbar_init(&bars->bf_full[i], 128);
+            mbar_init(&bars->stg_empty[i], kConvThreads);
+            mbar_init(&bars->bf_full[i], kConvThreads);
             mbar_init(&bars->bf_empty[i], 1);
         }
         for (int i = 0; i < kSBufs; ++i) {
@@ -370,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             bool ok = true;
 
             // prepare tile i (iterator itp): my partial scores of tile i are returned in sr
-            auto prepare = [&](int64_t i, const TileIter& itp, uint32_t (&sr)[32]) -> bool {
+            auto prepare = [&](int64_t i, const TileIter& itp, uint32_t (&sr)[32]) __attribute__((always_inline)) -> bool {
                 const bool first = (i == 0) || itp.j == 0;
                 const int sb = int(i % kSBufs);
                 if (first) {
@@ -546,16 +548,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 advance(p, it);
             }
             MLA_PROF(wacc[14] = clock64() - t_loop0;)
-        } else if ((warp == 2 || warp == 3 || warp >= 8) && Tr::kConvert) {
+        } else if (warp == 2 || warp == 3) {
+          if constexpr (Tr::kConvert) {
             // ------------------------------------------------------------ fp32 -> bf16
             // Converts two fp32 half-tile staging buffers into one bf16 128B-swizzled
             // slot. Every thread reads its share of a half tile into registers and
             // releases the staging buffer before writing, so the next TMA load can
             // start at once.
-            const int ct = (warp < 4 ? (warp - 2) : (warp - 6)) * 32 + lane;
-            constexpr int kU = kStgRows * 32 / 128;   // c_kv units of 8 floats per thread per half tile
-            constexpr int kP = kStgRows * 8 / 128;    // pe units per thread per half tile (CTA 1)
-            static_assert(kU * 128 == kStgRows * 32 && kP * 128 == kStgRows * 8, "converter mapping");
+            const int ct = (warp - 2) * 32 + lane;
+            constexpr int kU = kStgRows * 32 / kConvThreads;   // c_kv units of 8 floats per thread per half tile
+            constexpr int kP = kStgRows * 8 / kConvThreads;    // pe units per thread per half tile (CTA 1)
+            static_assert(kU * kConvThreads == kStgRows * 32 && kP * kConvThreads == kStgRows * 8, "converter mapping");
             bool okc = true;
             for (int64_t i = 0; okc && i < n; ++i) {
                 const int sl = int(i % Tr::kSlots);
@@ -576,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     uint4 cv[kU], pv[kP];
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
-                        const int u = ct + q * 128, r = u >> 5, c8 = u & 31;
+                        const int u = ct + q * kConvThreads, r = u >> 5, c8 = u & 31;
                         const float4 a = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8);
                         const float4 b = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8 + 4);
                         cv[q] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
@@ -586,7 +589,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                         const float* pe = src + kStgRows * kHalf;
 #pragma unroll
                         for (int q = 0; q < kP; ++q) {
-                            const int u = ct + q * 128, r = u >> 3, c8 = u & 7;
+                            const int u = ct + q * kConvThreads, r = u >> 3, c8 = u & 7;
                             const float4 a = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8);
                             const float4 b = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8 + 4);
                             pv[q] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
@@ -599,14 +602,14 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     mbar_arrive(&bars->stg_empty[st]);
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
-                        const int u = ct + q * 128, r = h * kStgRows + (u >> 5), c8 = u & 31;
+                        const int u = ct + q * kConvThreads, r = h * kStgRows + (u >> 5), c8 = u & 31;
                         const int chunk = c8 >> 3, unit = (c8 & 7) ^ (r & 7);
                         *reinterpret_cast<uint4*>(buf + chunk * kChunkBytes + r * 128 + unit * 16) = cv[q];
                     }
                     if (rank == 1) {
 #pragma unroll
                         for (int q = 0; q < kP; ++q) {
-                            const int u = ct + q * 128, r = h * kStgRows + (u >> 3), c8 = u & 7;
+                            const int u = ct + q * kConvThreads, r = h * kStgRows + (u >> 3), c8 = u & 7;
                             const int unit = c8 ^ (r & 7);
                             *reinterpret_cast<uint4*>(buf + 4 * kChunkBytes + r * 128 + unit * 16) = pv[q];
                         }
@@ -616,6 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 fence_proxy_async_smem();
                 mbar_arrive(&bars->bf_full[sl]);
             }
+          }
         }
     }
 
@@ -826,9 +830,11 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                 cudaHostGetDevicePointer(reinterpret_cast<void**>(&p.trace), trace_host, 0);
             }
         }
-        if (cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p) != cudaSuccess) {
+        const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p);
+        if (le != cudaSuccess) {
             cudaGetLastError();
-            return set_error(MLA_ERR_CUDA, "MLA: launch of the tensor-core attention kernel failed");
+            return set_error(MLA_ERR_CUDA, "MLA: launch of the tensor-core attention kernel failed: %s",
+                             cudaGetErrorString(le));
         }
         MLA_TRY(check_launch("tensor-core attention"));
         if (trace_host) {
