@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     const int64_t t_end = min(t_begin + p.tiles_per_cluster, p.total_tiles);
     const int64_t n = t_end > t_begin ? t_end - t_begin : 0;   // tiles of this cluster
     volatile int* abort = &bars->abort;
-    MLA_PROF(long long wacc[16] = {0};)
+    MLA_PROF(long long wacc[18] = {0};)
     MLA_PROF(const long long t_kernel0 = clock64();)
 
     if (threadIdx.x == 0) {
@@ -309,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     const int sl = int(i % Tr::kSlots);
                     const uint32_t base = smem_slots + sl * kSlotBytes;
                     const uint32_t p_tmem = tmem + kTmemS + sb * NK;
+                    MLA_PROF(const long long tpv = clock64();)
                     for (int k = 0; k < NK / 16; ++k) {
                         // B = V [16 keys x 256 latent], MN-major, 128B swizzle:
                         // LBO = stride between 64-dim chunks, SBO = stride between 8-key groups.
@@ -317,6 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     }
                     mma_commit(&bars->bf_empty[sl]);
                     mma_commit(&bars->o_done[sb]);
+                    MLA_PROF(wacc[16] += clock64() - tpv;)
                     return true;
                 };
                 for (int64_t i = 0; i < n && ok; ++i) {
@@ -334,12 +336,14 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     tc_fence_after();
                     const uint32_t base = smem_slots + sl * kSlotBytes;
                     const int sb = int(i % kSBufs);
+                    MLA_PROF(const long long tsi = clock64();)
                     for (int k = 0; k < dims / 16; ++k) {
                         // B = K [32 keys x 16 dims], K-major, 128B swizzle: chunk k/4, +32 B per k-step.
                         const uint64_t bd = smem_desc(base + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024, 2);
                         mma_ts(tmem + kTmemS + sb * NK, tmem + kTmemQ + k * 8, bd, idesc_s, k > 0 ? 1u : 0u);
                     }
                     mma_commit(&bars->s_full[sb]);
+                    MLA_PROF(wacc[17] += clock64() - tsi;)
                     trace_put(p, 1, i * 16 + 2);
                     first_ring[i % kSBufs] = first;
                     if (i >= 2) ok = issue_pv(i - 2, first_ring[(i - 2) % kSBufs]);
@@ -556,9 +560,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             // releases the staging buffer before writing, so the next TMA load can
             // start at once.
             const int ct = (warp - 2) * 32 + lane;
-            constexpr int kU = kStgRows * 32 / kConvThreads;   // c_kv units of 8 floats per thread per half tile
-            constexpr int kP = kStgRows * 8 / kConvThreads;    // pe units per thread per half tile (CTA 1)
-            static_assert(kU * kConvThreads == kStgRows * 32 && kP * kConvThreads == kStgRows * 8, "converter mapping");
+            // Lanes take consecutive 16-byte (4 x fp32) pieces of a staging row, so a
+            // warp's shared-memory reads are dense; each piece becomes 8 bytes of bf16.
+            constexpr int kU = kStgRows * (kHalf / 4) / kConvThreads;   // c_kv float4 pieces per thread
+            constexpr int kP = kStgRows * (kRope / 4) / kConvThreads;   // pe float4 pieces per thread (CTA 1)
+            static_assert(kU * kConvThreads == kStgRows * (kHalf / 4) && kP * kConvThreads == kStgRows * (kRope / 4),
+                          "converter mapping");
             bool okc = true;
             for (int64_t i = 0; okc && i < n; ++i) {
                 const int sl = int(i % Tr::kSlots);
@@ -575,25 +582,19 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                         okc = false;
                         break;
                     }
-                    const float* src = reinterpret_cast<const float*>(stg + st * kStgBytes);
-                    uint4 cv[kU], pv[kP];
+                    const float4* src = reinterpret_cast<const float4*>(stg + st * kStgBytes);
+                    uint2 cv[kU], pv[kP];
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
-                        const int u = ct + q * kConvThreads, r = u >> 5, c8 = u & 31;
-                        const float4 a = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8);
-                        const float4 b = *reinterpret_cast<const float4*>(src + r * kHalf + c8 * 8 + 4);
-                        cv[q] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
-                                           pack_bf16(b.z, b.w));
+                        const float4 a = src[ct + q * kConvThreads];
+                        cv[q] = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
                     }
                     if (rank == 1) {
-                        const float* pe = src + kStgRows * kHalf;
+                        const float4* pe = src + kStgRows * (kHalf / 4);
 #pragma unroll
                         for (int q = 0; q < kP; ++q) {
-                            const int u = ct + q * kConvThreads, r = u >> 3, c8 = u & 7;
-                            const float4 a = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8);
-                            const float4 b = *reinterpret_cast<const float4*>(pe + r * kRope + c8 * 8 + 4);
-                            pv[q] = make_uint4(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w), pack_bf16(b.x, b.y),
-                                               pack_bf16(b.z, b.w));
+                            const float4 a = pe[ct + q * kConvThreads];
+                            pv[q] = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
                         }
                     }
                     // my generic-proxy reads of the staging buffer must be ordered before
@@ -602,16 +603,18 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     mbar_arrive(&bars->stg_empty[st]);
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
-                        const int u = ct + q * kConvThreads, r = h * kStgRows + (u >> 5), c8 = u & 31;
-                        const int chunk = c8 >> 3, unit = (c8 & 7) ^ (r & 7);
-                        *reinterpret_cast<uint4*>(buf + chunk * kChunkBytes + r * 128 + unit * 16) = cv[q];
+                        const int f = ct + q * kConvThreads;          // float4 index in the half tile
+                        const int r = h * kStgRows + (f >> 6), c4 = f & 63;
+                        const int chunk = c4 >> 4, unit = ((c4 & 15) >> 1) ^ (r & 7);
+                        *reinterpret_cast<uint2*>(buf + chunk * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = cv[q];
                     }
                     if (rank == 1) {
 #pragma unroll
                         for (int q = 0; q < kP; ++q) {
-                            const int u = ct + q * kConvThreads, r = h * kStgRows + (u >> 3), c8 = u & 7;
-                            const int unit = c8 ^ (r & 7);
-                            *reinterpret_cast<uint4*>(buf + 4 * kChunkBytes + r * 128 + unit * 16) = pv[q];
+                            const int f = ct + q * kConvThreads;
+                            const int r = h * kStgRows + (f >> 4), c4 = f & 15;
+                            const int unit = (c4 >> 1) ^ (r & 7);
+                            *reinterpret_cast<uint2*>(buf + 4 * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = pv[q];
                         }
                     }
                 }
@@ -631,6 +634,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             for (int k = 0; k < 15; ++k)
                 if (wacc[k]) trace_put(p, 8 + k, wacc[k] / 1000);
         if (threadIdx.x == 0) trace_put(p, 23, (clock64() - t_kernel0) / 1000);
+        if (warp == 1 && lane == 0) {
+            trace_put(p, 24, wacc[16] / 1000);
+            trace_put(p, 25, wacc[17] / 1000);
+        }
     }
 #endif
     if (threadIdx.x == 0) trace_put(p, 4, 1);
@@ -849,9 +856,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                 const volatile int* t = trace_host + b * 32;
                 fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d | kcyc total %d "
                         "stg_empty %d bf_empty(p) %d p_full %d q_ready %d bf_full %d s_full %d x_full %d o_resc %d "
-                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d\n",
+                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d pv_issue %d s_issue %d\n",
                         (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[23], t[8], t[9], t[10], t[11], t[12],
-                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22]);
+                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25]);
             }
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);
