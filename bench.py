@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--min-warmup-s", type=float, default=1.5,
                     help="minimum warm-up wall time (lets the clock sampler start); 0 under a profiler")
     ap.add_argument("--no-stages", action="store_true", help="skip the per-stage / per-precision timings")
+    ap.add_argument("--shard", default=None, choices=["batch", "keys"],
+                    help="multi-GPU layout: batch (weak scaling, default) or keys (strong scaling, default for c2)")
     return ap.parse_args()
 
 
@@ -137,9 +139,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+KEY_SHARDED = {"on": False}
+
+
 def run_forward(mcc, t, w, precision):
     qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
                                w.nope, w.rope, mc.EPS, precision=precision)
+    if KEY_SHARDED["on"]:
+        # every rank holds all sequences' queries and its own key slice; partial
+        # attention, NCCL all-gather of (out, lse), exact log-sum-exp merge
+        from mla_custom_cuda import sharding
+        return sharding.sk_sharded_attention(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
+                                             precision=precision), qa, qr
     return mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, causal=w.causal,
                                 precision=precision), qa, qr
 
@@ -214,7 +225,20 @@ def main_ours(args):
     w = mc.CONFIGS[args.config]
     precision = args.precision
     B = w.batch
-    t = mc.make_inputs(w, device=dev, gen="device", seed=1234 + rank)
+    shard = args.shard or ("keys" if args.config == "c2" else "batch")
+    if world == 1:
+        shard = "batch"
+    if shard == "keys":
+        if w.causal:
+            raise SystemExit("key sharding is for non-causal decode")
+        from mla_custom_cuda import sharding
+        k0, k1 = sharding.key_shard(w.sk, rank, world)
+        t = mc.make_inputs(w, device=dev, gen="device", seed=1234)   # same queries / weights on every rank
+        t["c_kv"] = t["c_kv"][:, k0:k1].contiguous()
+        t["pe_cache"] = t["pe_cache"][:, k0:k1].contiguous()
+        KEY_SHARDED["on"] = True
+    else:
+        t = mc.make_inputs(w, device=dev, gen="device", seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -260,7 +284,7 @@ def main_ours(args):
         tt = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
         ms = float(tt.item())
-    tokens_total = B * w.sq * world
+    tokens_total = B * w.sq * (world if shard == "batch" else 1)
     value = tokens_total / (ms * 1e-3)
 
     # ---- per-stage timing (same stream, CUDA events; inputs larger than L2)
@@ -329,13 +353,13 @@ def main_ours(args):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "us_per_layer": ms * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "weak" if shard == "batch" else "strong", "vs_baseline": None,
             "dtype": dtype_name if precision == "exact" else
                      ("bf16" if w.dtype != torch.float16 else "f16") + " tensor-core operands, f32 accumulate, "
                      + dtype_name + " storage",
             "data": "synthetic (seeded N(0,1) cache / activations, N(0,0.02) weights)",
-            "config": {**w.describe(), "global_batch": B * world, "precision": precision,
-                       "parallelism": f"batch-shard dp{world}",
+            "config": {**w.describe(), "global_batch": B * (world if shard == "batch" else 1), "precision": precision,
+                       "parallelism": f"batch-shard dp{world}" if shard == "batch" else f"key-shard sp{world} (NCCL all-gather + LSE merge)",
                        "l2": "inputs larger than L2 (cache %.2f GB per GPU)" % (cache_b / 1e9)},
             "stages": stages,
             "roofline": {"bound": "hbm", "kernel": "mla_attention (cache read)",

@@ -146,6 +146,36 @@ MLA_API mla_status_t mla_attention(
     void* out,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------ key-sharded attention --
+ * No counterpart in the reference (it is single-GPU). For long contexts the
+ * keys of every sequence can be split across GPUs: each GPU runs
+ * mla_attention_partial on its key shard, the shards' outputs and lse are
+ * gathered (NCCL all-gather), and mla_lse_combine merges them. The merge is
+ * exact because the W_uv projection is linear in the normalised context.
+ *
+ * mla_attention_partial: same operands, workspace and semantics as
+ * mla_attention (without causal masking), plus
+ *   lse  [batch, sq, heads] fp32: natural-log sum of exp(score / scale) over
+ *        this shard's keys (-inf for an empty shard).
+ * mla_lse_combine: outs [parts, rows, v_dim] and lses [parts, rows] (rows =
+ * batch*sq*heads) -> out [rows, v_dim] (and lse_out [rows] if not NULL);
+ * fp32 / fp16 / bf16.
+ */
+MLA_API mla_status_t mla_attention_partial(
+    mla_dtype_t dtype, mla_precision_t precision,
+    const void* q_absorbed, const void* q_rope,
+    const void* c_kv, const void* pe_cache, const void* W_uv,
+    int64_t batch, int64_t sq, int64_t sk, int64_t heads,
+    int64_t kv_rank, int64_t rope, int64_t v_dim,
+    double scale,
+    void* out, float* lse,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+MLA_API mla_status_t mla_lse_combine(
+    mla_dtype_t dtype, int64_t parts, int64_t rows, int64_t v_dim,
+    const void* outs, const float* lses,
+    void* out, float* lse_out, void* stream);
+
 /* ------------------------------------------------- allocation-free variant --
  * No counterpart in the reference. Same computation as mla_attention with
  * MLA_PREC_TENSOR (fp32, fp16 or bf16 storage; heads 128, kv_rank 512,

@@ -5,6 +5,7 @@
 // performs none).
 #include "qprep.cuh"
 #include "tc.cuh"
+#include "lse_combine.cuh"
 
 #include <cstdarg>
 #include <cstdio>
@@ -177,10 +178,12 @@ mla_status_t mla_attention_workspace_size(mla_dtype_t dtype, mla_precision_t pre
     return MLA_OK;
 }
 
-mla_status_t mla_attention(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed, const void* q_rope,
+}  // extern "C"
+
+static mla_status_t attention_impl(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed, const void* q_rope,
                            const void* c_kv, const void* pe_cache, const void* W_uv, int64_t batch, int64_t sq,
                            int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim, double scale,
-                           int causal, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+                           int causal, void* out, float* lse, void* workspace, size_t workspace_bytes, void* stream) {
     MLA_TRY(validate_a(dtype, precision, batch, sq, sk, heads, kv_rank, rope, v_dim, causal));
     if (batch * sq == 0) return MLA_OK;
     if (!out || !W_uv || !q_absorbed) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: null pointer");
@@ -190,13 +193,14 @@ mla_status_t mla_attention(mla_dtype_t dtype, mla_precision_t precision, const v
         const size_t esz = dtype == MLA_DTYPE_F64 ? 8 : dtype == MLA_DTYPE_F32 ? 4 : 2;
         if (cudaMemsetAsync(out, 0, size_t(batch * sq * heads * v_dim) * esz, st) != cudaSuccess)
             return set_error(MLA_ERR_CUDA, "MLA mla_attention: memset failed");
+        if (lse) return fill_neg_inf(lse, batch * sq * heads, st);   // an empty shard weighs nothing
         return MLA_OK;
     }
     if (!c_kv || (rope > 0 && (!q_rope || !pe_cache)))
         return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: null operand pointer");
     if (scale == 0.0) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: scale must be non-zero");
     AArgs a{q_absorbed, q_rope, c_kv, pe_cache, W_uv, batch, sq, sk, heads, kv_rank, rope, v_dim,
-            scale, causal, out, workspace, workspace_bytes};
+            scale, causal, out, workspace, workspace_bytes, lse};
     const bool tc = use_tc_attention(dtype, precision, a);
     const size_t need = tc ? dispatch(dtype, [&](auto t) { return tc_attention_workspace<decltype(t)>(a); })
                            : dispatch(dtype, [&](auto t) { return attn_exact_workspace<decltype(t)>(a); });
@@ -205,6 +209,41 @@ mla_status_t mla_attention(mla_dtype_t dtype, mla_precision_t precision, const v
                          workspace ? workspace_bytes : size_t(0));
     if (tc) return dispatch(dtype, [&](auto t) { return tc_attention<decltype(t)>(a, st); });
     return dispatch(dtype, [&](auto t) { return attn_exact<decltype(t)>(a, st); });
+}
+
+extern "C" {
+
+mla_status_t mla_attention(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed, const void* q_rope,
+                           const void* c_kv, const void* pe_cache, const void* W_uv, int64_t batch, int64_t sq,
+                           int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim, double scale,
+                           int causal, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    return attention_impl(dtype, precision, q_absorbed, q_rope, c_kv, pe_cache, W_uv, batch, sq, sk, heads, kv_rank,
+                          rope, v_dim, scale, causal, out, nullptr, workspace, workspace_bytes, stream);
+}
+
+mla_status_t mla_attention_partial(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed,
+                                   const void* q_rope, const void* c_kv, const void* pe_cache, const void* W_uv,
+                                   int64_t batch, int64_t sq, int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope,
+                                   int64_t v_dim, double scale, void* out, float* lse, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    if (!lse) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention_partial: lse must not be NULL");
+    return attention_impl(dtype, precision, q_absorbed, q_rope, c_kv, pe_cache, W_uv, batch, sq, sk, heads, kv_rank,
+                          rope, v_dim, scale, 0, out, lse, workspace, workspace_bytes, stream);
+}
+
+mla_status_t mla_lse_combine(mla_dtype_t dtype, int64_t parts, int64_t rows, int64_t v_dim, const void* outs,
+                             const float* lses, void* out, float* lse_out, void* stream) {
+    if (dtype < MLA_DTYPE_F32 || dtype > MLA_DTYPE_BF16)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: unknown dtype %d", int(dtype));
+    if (parts <= 0 || rows < 0 || v_dim <= 0)
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_lse_combine: invalid sizes (parts=%lld rows=%lld v=%lld)",
+                         (long long)parts, (long long)rows, (long long)v_dim);
+    if (rows == 0) return MLA_OK;
+    if (!outs || !lses || !out) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_lse_combine: null pointer");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return dispatch(dtype, [&](auto t) {
+        return lse_combine<decltype(t)>(parts, rows, v_dim, outs, lses, out, lse_out, st);
+    });
 }
 
 }  // extern "C"

@@ -195,7 +195,8 @@ template <class Cfg, typename T>
 __global__ void __launch_bounds__(256) out_kernel(
     const typename Cfg::Acc* __restrict__ O_part, const typename Cfg::Acc* __restrict__ l_part,
     const T* __restrict__ W_uv, T* __restrict__ out,
-    int64_t M, int64_t heads, int64_t R, int64_t V, int64_t rows_total, int splits)
+    int64_t M, int64_t heads, int64_t R, int64_t V, int64_t rows_total, int splits,
+    const typename Cfg::Acc* __restrict__ row_max, float* __restrict__ lse)
 {
     using Acc = typename Cfg::Acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -210,6 +211,11 @@ __global__ void __launch_bounds__(256) out_kernel(
             for (int z = 0; z < splits; ++z) l += l_part[int64_t(z) * rows_total + (m0 + i) * heads + h];
         }
         inv_l_s[i] = (l > Acc(0)) ? Acc(1) / l : Acc(0);
+        // partial attention: log-sum-exp of the row's scaled scores
+        if (lse && l_part && blockIdx.x == 0 && m0 + i < M) {
+            const int64_t g = (m0 + i) * heads + h;
+            lse[g] = float(row_max[g] + log(l));
+        }
     }
     __syncthreads();
     OutProblem<T, Acc> p{O_part, inv_l_s, W_uv, M, heads, R, V, rows_total, h, m0,
@@ -313,13 +319,13 @@ mla_status_t run_scores_pv(const AArgs& a, const APlan& p, typename Cfg::Acc* S,
 
 template <class Cfg, typename T>
 mla_status_t run_out(const AArgs& a, const APlan& p, const typename Cfg::Acc* O, const typename Cfg::Acc* l,
-                     cudaStream_t st) {
+                     cudaStream_t st, const typename Cfg::Acc* row_max = nullptr) {
     auto kern = out_kernel<Cfg, T>;
     set_smem<Cfg>(kern);
     const int64_t M = a.batch * a.sq;
     dim3 grid(unsigned(ceil_div(a.v_dim, Cfg::BN)), unsigned(ceil_div(M, Cfg::BM)), unsigned(a.heads));
     kern<<<grid, 256, Cfg::kSmemBytes, st>>>(O, l, static_cast<const T*>(a.W_uv), static_cast<T*>(a.out), M,
-                                             a.heads, a.kv_rank, a.v_dim, p.rows_total, p.splits);
+                                             a.heads, a.kv_rank, a.v_dim, p.rows_total, p.splits, row_max, a.lse);
     return check_launch("attention W_uv output");
 }
 
@@ -361,8 +367,8 @@ mla_status_t attn_exact(const AArgs& a, cudaStream_t st) {
     } else {
         MLA_TRY((run_scores_pv<CfgBig<Acc>, T>(a, p, S, tmax, rmax, O, l, st)));
     }
-    if (p.small_out) return run_out<CfgSmall<Acc>, T>(a, p, O, l, st);
-    return run_out<CfgBig<Acc>, T>(a, p, O, l, st);
+    if (p.small_out) return run_out<CfgSmall<Acc>, T>(a, p, O, l, st, rmax);
+    return run_out<CfgBig<Acc>, T>(a, p, O, l, st, rmax);
 }
 
 template size_t attn_exact_workspace<float>(const AArgs&);

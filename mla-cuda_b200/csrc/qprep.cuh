@@ -24,6 +24,7 @@ struct AArgs {
     int causal;
     void* out;
     void* workspace; size_t workspace_bytes;
+    float* lse;   // optional [B*Sq*H]: natural-log sum of exp(score) per row (partial attention)
 };
 
 template <typename T> size_t qprep_exact_workspace(const QArgs& a);

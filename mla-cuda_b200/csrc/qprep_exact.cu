@@ -108,10 +108,10 @@ __global__ void __launch_bounds__(256) lat_norm_kernel(
 template <typename T>
 struct RopeTable { acc_t<T> inv_freq[kMaxRopePairs]; };
 
-template <typename T>
+template <typename T, typename NopeT = acc_t<T>>
 __global__ void __launch_bounds__(256) rope_gather_kernel(
     const acc_t<T>* __restrict__ P2, int splits, const int64_t* __restrict__ positions,
-    acc_t<T>* __restrict__ q_nope, T* __restrict__ q_rope,
+    NopeT* __restrict__ q_nope, T* __restrict__ q_rope,
     int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, RopeTable<T> tab)
 {
     using Acc = acc_t<T>;
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(256) rope_gather_kernel(
             return v;
         };
         if (e < nope) {
-            q_nope[mh * nope + e] = sum(col);
+            q_nope[mh * nope + e] = cvt<NopeT>(sum(col));
         } else {
             const int64_t j = e - nope;
             const Acc ev = sum(col), od = sum(col + 1);
@@ -328,9 +328,8 @@ template mla_status_t qprep_exact<__nv_bfloat16>(const QArgs&, cudaStream_t);
 // ------------------------------------------------------------ tensor-core Q-prep
 // MLA_PREC_TENSOR: 2a1 and 2a2 run as split-K tcgen05 GEMMs (kind::tf32 for
 // fp32 storage, kind::f16 for 16-bit) writing fp32 partials that the same
-// RMSNorm and RoPE kernels reduce; 2c is a per-head tcgen05 GEMM for fp32
-// storage (its fp32 left operand needs fp32 weights) and the CUDA-core kernel
-// otherwise.
+// RMSNorm and RoPE kernels reduce; 2c is a per-head tcgen05 GEMM whose left
+// operand, q_nope, is rounded to the storage dtype.
 namespace {
 
 struct QTPlan {
@@ -379,7 +378,7 @@ bool qprep_tensor_supported(const QArgs& a) {
         constexpr int64_t v = 16 / sizeof(T);   // TMA: 16-byte strides
         const int64_t ncols = a.heads * (a.nope + a.rope);
         return a.q_lora % 32 == 0 && ncols % 32 == 0 && a.kv_rank % 32 == 0 && a.hidden % v == 0 &&
-               a.q_lora % v == 0 && a.nope % 4 == 0 && a.batch * a.sq > 0;
+               a.q_lora % v == 0 && a.nope % v == 0 && a.batch * a.sq > 0;
     }
 }
 
@@ -397,7 +396,7 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
     Acc* P1 = reinterpret_cast<Acc*>(ws + p.off_p1);
     T* q_lat = reinterpret_cast<T*>(ws + p.off_qlat);
     Acc* P2 = reinterpret_cast<Acc*>(ws + p.off_p2);
-    Acc* q_nope = reinterpret_cast<Acc*>(ws + p.off_qnope);
+    T* q_nope_t = reinterpret_cast<T*>(ws + p.off_qnope);
     if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
         return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
 
@@ -432,28 +431,22 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
         const int64_t cap = 16LL * sm_count();
         if (blocks > cap) blocks = cap;
         if (blocks < 1) blocks = 1;
-        rope_gather_kernel<T><<<unsigned(blocks), 256, 0, st>>>(P2, p.split2, a.positions, q_nope,
-                                                                 static_cast<T*>(a.q_rope), M, a.sq, a.heads, a.nope,
-                                                                 a.rope, tab);
+        // q_nope in the storage dtype: the left operand of the 2c tensor-core GEMM,
+        // whose operands share one dtype
+        rope_gather_kernel<T, T><<<unsigned(blocks), 256, 0, st>>>(P2, p.split2, a.positions, q_nope_t,
+                                                                    static_cast<T*>(a.q_rope), M, a.sq, a.heads,
+                                                                    a.nope, a.rope, tab);
         MLA_TRY(check_launch("q rope (2b)"));
     }
-    if constexpr (std::is_same<T, float>::value) {
-        TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h]
-        g3.A = q_nope; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;
-        g3.a_ld[0] = a.nope; g3.a_ld[1] = a.heads * a.nope;
-        g3.B = a.W_uk; g3.b_mn = true; g3.b_dims[0] = a.kv_rank; g3.b_dims[1] = a.nope; g3.b_dims[2] = a.heads;
-        g3.b_ld[0] = a.kv_rank; g3.b_ld[1] = a.nope * a.kv_rank;
-        g3.M = M; g3.N = a.kv_rank; g3.K = a.nope; g3.Z = int(a.heads); g3.split = false; g3.k_chunk = a.nope;
-        g3.C = a.q_absorbed; g3.c_is_t = true; g3.c_ldm = a.heads * a.kv_rank; g3.c_ldz = a.kv_rank;
-        g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err;
-        return tc_gemm<T>(g3, st);
-    } else {
-        if (M <= 16)
-            return launch_absorb<CfgSmall<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk),
-                                                   static_cast<T*>(a.q_absorbed), a, M, st);
-        return launch_absorb<CfgBig<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk), static_cast<T*>(a.q_absorbed),
-                                             a, M, st);
-    }
+    TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h]
+    g3.A = q_nope_t; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;
+    g3.a_ld[0] = a.nope; g3.a_ld[1] = a.heads * a.nope;
+    g3.B = a.W_uk; g3.b_mn = true; g3.b_dims[0] = a.kv_rank; g3.b_dims[1] = a.nope; g3.b_dims[2] = a.heads;
+    g3.b_ld[0] = a.kv_rank; g3.b_ld[1] = a.nope * a.kv_rank;
+    g3.M = M; g3.N = a.kv_rank; g3.K = a.nope; g3.Z = int(a.heads); g3.split = false; g3.k_chunk = a.nope;
+    g3.C = a.q_absorbed; g3.c_is_t = true; g3.c_ldm = a.heads * a.kv_rank; g3.c_ldz = a.kv_rank;
+    g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err;
+    return tc_gemm<T>(g3, st);
 }
 
 #define MLA_QT(T) \

@@ -661,7 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
 // Combine the segments of every (group, head) row into a normalised context.
 // One warp per row; the cluster segments covering group g are contiguous.
 template <typename OutT>
-__global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups)
+__global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups,
+                                                      float* __restrict__ lse)
 {
     const int64_t rowid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
@@ -693,6 +694,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __re
         for (int e = 0; e < 16; ++e) acc[e] += w * src[e * 32 + lane];
     }
     const float inv = 1.f / L;
+    // log-sum-exp of the row's scaled scores (M and log2(L) are in log2 units)
+    if (lse && lane == 0) lse[rowid] = (M + log2f(L)) * 0.69314718055994531f;
     OutT* dst = O_norm + rowid * kRank;
     for (int e = 0; e < 16; ++e) dst[e * 32 + lane] = cvt<OutT>(acc[e] * inv);
 }
@@ -866,13 +869,13 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         const int64_t rows_total = pl.groups * kHeads;
         const unsigned cblocks = unsigned((rows_total * 32 + 255) / 256);
         if (a.v_dim % 32 != 0) {   // W_uv projection on CUDA cores from an fp32 context
-            combine_kernel<float><<<cblocks, 256, 0, st>>>(p, O_norm, pl.groups);
+            combine_kernel<float><<<cblocks, 256, 0, st>>>(p, O_norm, pl.groups, a.lse);
             MLA_TRY(check_launch("segment combine"));
             return attn_out_normalized<T>(a, O_norm, st);
         }
         // context in the storage dtype, then out[:, h] = ctx[:, h] @ W_uv[h]^T on the tensor cores
         T* ctx = reinterpret_cast<T*>(O_norm);
-        combine_kernel<T><<<cblocks, 256, 0, st>>>(p, ctx, pl.groups);
+        combine_kernel<T><<<cblocks, 256, 0, st>>>(p, ctx, pl.groups, a.lse);
         MLA_TRY(check_launch("segment combine"));
         TcGemm g{};
         g.A = ctx; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;

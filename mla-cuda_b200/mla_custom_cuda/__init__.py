@@ -35,6 +35,7 @@ import torch
 
 __all__ = [
     "q_absorbed", "mla_attention", "q_absorbed_ex", "mla_attention_ex",
+    "mla_attention_partial", "lse_combine",
     "set_precision", "get_precision", "library_path", "abi_version",
 ]
 
@@ -70,6 +71,11 @@ def _load() -> ctypes.CDLL:
     lib.mla_attention.restype = ctypes.c_int
     lib.mla_attention.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_vp] * 5 + [_c_i64] * 7
                                   + [ctypes.c_double, ctypes.c_int, _c_vp, _c_vp, _c_size, _c_vp])
+    lib.mla_attention_partial.restype = ctypes.c_int
+    lib.mla_attention_partial.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_vp] * 5 + [_c_i64] * 7
+                                          + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
+    lib.mla_lse_combine.restype = ctypes.c_int
+    lib.mla_lse_combine.argtypes = [ctypes.c_int] + [_c_i64] * 3 + [_c_vp] * 5
     return lib
 
 
@@ -232,3 +238,55 @@ def mla_attention(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float) -> tor
     [B,Sq,H,v_dim] tensor in the input dtype.
     """
     return mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale)
+
+
+def mla_attention_partial(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float,
+                          precision: Optional[str] = None):
+    """Attention over a shard of the keys: returns (out [B,Sq,H,V], lse [B,Sq,H]
+    fp32), lse being the natural-log sum of exp(score) over this shard's keys.
+    Shards are merged exactly by lse_combine (no counterpart in the reference)."""
+    dtype, device = _float_operands([("q_absorbed", q_absorbed), ("q_rope", q_rope), ("c_kv", c_kv),
+                                     ("pe_cache", pe_cache), ("W_uv", W_uv)])
+    _check(q_absorbed.dim() == 4, "q_absorbed must be [B,Sq,H,kv_rank]")
+    B, Sq, H, R = q_absorbed.shape
+    D = q_rope.shape[3]
+    _check(tuple(q_rope.shape[:3]) == (B, Sq, H), "q_rope must be [B,Sq,H,rope]")
+    _check(c_kv.dim() == 3 and c_kv.shape[0] == B and c_kv.shape[2] == R, "c_kv must be [B,Sk,kv_rank]")
+    Sk = c_kv.shape[1]
+    _check(tuple(pe_cache.shape) == (B, Sk, D), "pe_cache must be [B,Sk,rope]")
+    _check(W_uv.dim() == 3 and W_uv.shape[0] == H and W_uv.shape[2] == R, "W_uv must be [H,v_dim,kv_rank]")
+    V = W_uv.shape[1]
+    qa, qr, ck, pe, wv = (t.contiguous() for t in (q_absorbed, q_rope, c_kv, pe_cache, W_uv))
+    out = torch.empty((B, Sq, H, V), dtype=dtype, device=device)
+    lse = torch.empty((B, Sq, H), dtype=torch.float32, device=device)
+    dt, pc = _DTYPE_CODES[dtype], _prec_code(precision)
+    nbytes = _c_size(0)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_attention_workspace_size(dt, pc, B, Sq, Sk, H, R, D, V, 0, ctypes.byref(nbytes)),
+                      "mla_attention_partial")
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=device)
+        st = _lib.mla_attention_partial(dt, pc, qa.data_ptr(), qr.data_ptr(), ck.data_ptr(), pe.data_ptr(),
+                                        wv.data_ptr(), B, Sq, Sk, H, R, D, V, float(scale), out.data_ptr(),
+                                        lse.data_ptr(), ws.data_ptr(), ws.numel(),
+                                        torch.cuda.current_stream(device).cuda_stream)
+    _raise_status(st, "mla_attention_partial")
+    return out, lse
+
+
+def lse_combine(outs: torch.Tensor, lses: torch.Tensor):
+    """Merge key-shard partials: outs [P, ..., V], lses [P, ...] fp32 ->
+    (out [..., V], lse [...]), out = sum_p exp(lse_p - L) outs_p."""
+    dtype, device = _float_operands([("outs", outs)])
+    _check(lses.is_cuda and lses.dtype == torch.float32, "lses must be a CUDA float32 tensor")
+    _check(tuple(outs.shape[:-1]) == tuple(lses.shape), "outs must be [P, ..., V] with lses [P, ...]")
+    P, V = outs.shape[0], outs.shape[-1]
+    rows = lses[0].numel()
+    o = outs.contiguous()
+    l = lses.contiguous()
+    out = torch.empty(outs.shape[1:], dtype=dtype, device=device)
+    lse = torch.empty(lses.shape[1:], dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        st = _lib.mla_lse_combine(_DTYPE_CODES[dtype], P, rows, V, o.data_ptr(), l.data_ptr(), out.data_ptr(),
+                                  lse.data_ptr(), torch.cuda.current_stream(device).cuda_stream)
+    _raise_status(st, "lse_combine")
+    return out, lse

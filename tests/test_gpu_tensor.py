@@ -141,3 +141,24 @@ def test_tc_forward_c0_vs_reference(mcc):
     out = mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], mc.SCALE, precision="tensor")
     assert rel_l2(qa.cpu(), d["qa64_full"]) < TOL
     assert rel_l2(out.cpu(), d["out64_full"]) < TOL
+
+
+@pytest.mark.parametrize("precision", ["exact", "tensor"])
+@pytest.mark.parametrize("parts", [2, 4])
+def test_key_shards_partial_and_combine(mcc, precision, parts):
+    """Key sharding emulated on one GPU: partial attention per key shard plus the
+    log-sum-exp merge equals attention over all keys; lse matches the oracle."""
+    from mla_custom_cuda import sharding
+    qa, qr, ck, pe, wuv = (t.to(DEV) for t in mc.attention_inputs(3, 2, 2000, seed=8))
+    outs, lses = [], []
+    for r in range(parts):
+        k0, k1 = sharding.key_shard(2000, r, parts)
+        o, l = mcc.mla_attention_partial(qa, qr, ck[:, k0:k1], pe[:, k0:k1], wuv, mc.SCALE, precision=precision)
+        outs.append(o)
+        lses.append(l)
+    merged, L = mcc.lse_combine(torch.stack(outs), torch.stack(lses))
+    full = mcc.mla_attention_ex(qa, qr, ck, pe, wuv, mc.SCALE, precision=precision)
+    tol = 1e-5 if precision == "exact" else TOL
+    assert rel_l2(merged, full) < tol
+    _, ref_lse = orc.mla_attention_partial(*(t.double().cpu() for t in (qa, qr, ck, pe, wuv)), mc.SCALE)
+    assert rel_l2(L.cpu(), ref_lse) < (1e-6 if precision == "exact" else 1e-3)

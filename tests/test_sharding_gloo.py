@@ -1,0 +1,74 @@
+"""Multi-rank host logic of the sharded layouts, on CPU ranks with gloo:
+key-shard ranges, the all-gather of partials in rank order and the exact
+log-sum-exp merge (with the oracle's partial attention standing in for the GPU
+kernel), and batch-shard ranges."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG, ROOT, rel_l2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import mla_configs as mc
+        from mla_custom_cuda import sharding
+        from oracle import mla_oracle as orc
+        qa, qr, ck, pe, wuv = (t.double() for t in mc.attention_inputs(2, 2, 97, seed=21))
+        k0, k1 = sharding.key_shard(97, rank, world)
+        out, lse = orc.mla_attention_partial(qa, qr, ck[:, k0:k1], pe[:, k0:k1], wuv, mc.SCALE)
+        outs, lses = sharding.gather_partials(out, lse)
+        merged, L = orc.lse_combine(outs, lses)
+        full = orc.mla_attention(qa, qr, ck, pe, wuv, mc.SCALE)
+        _, full_lse = orc.mla_attention_partial(qa, qr, ck, pe, wuv, mc.SCALE)
+        result_q.put((rank, rel_l2(merged, full), rel_l2(L, full_lse)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_key_sharded_merge_on_gloo(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get() for _ in range(world))
+    for rank, e_out, e_lse in res:
+        assert e_out < 1e-12 and e_lse < 1e-12, (rank, e_out, e_lse)
+
+
+def test_shard_ranges_cover_exactly():
+    from mla_custom_cuda import sharding
+    for n, world in [(65536, 8), (4989, 3), (7, 4), (0, 2), (128, 8)]:
+        spans = [sharding.key_shard(n, r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        sizes = [e - s for s, e in spans]
+        assert max(sizes) - min(sizes) <= 1
+        assert sharding.batch_shard(n, 0, world) == spans[0]
+    with pytest.raises(ValueError):
+        sharding.key_shard(10, 4, 4)
