@@ -219,6 +219,7 @@ def main_ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import torch.distributed as dist
+        os.environ.setdefault("NCCL_DEBUG", "WARN")   # keep NCCL's banner off stdout (one JSON line)
         dist.init_process_group("nccl", device_id=dev)
     import mla_custom_cuda as mcc
 
