@@ -358,7 +358,7 @@ QTPlan make_tplan(const QArgs& a) {
     const int64_t bk = tc_gemm_bk<T>();
     const int64_t mt = ceil_div(M, 128);
     p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), a.hidden, bk, 1, p.chunk1);
-    p.split2 = tc_split(mt * ceil_div(ncols, 256), a.q_lora, bk, 2, p.chunk2);
+    p.split2 = tc_split(mt * ceil_div(ncols, 128), a.q_lora, bk, 1, p.chunk2);
     size_t off = 0;
     p.off_err = off;   off = align_up(off + 256, 256);
     p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(Acc), 256);
@@ -417,7 +417,7 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
     g2.B = a.W_q_b; g2.b_mn = true; g2.b_dims[0] = ncols; g2.b_dims[1] = a.q_lora; g2.b_dims[2] = 1;
     g2.b_ld[0] = ncols; g2.b_ld[1] = ncols * a.q_lora;
     g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = p.split2; g2.split = true; g2.k_chunk = p.chunk2;
-    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 256; g2.err = err;
+    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err;
     MLA_TRY(tc_gemm<T>(g2, st));
 
     RopeTable<T> tab{};
