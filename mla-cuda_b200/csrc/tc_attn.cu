@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     const int64_t t_end = min(t_begin + p.tiles_per_cluster, p.total_tiles);
     const int64_t n = t_end > t_begin ? t_end - t_begin : 0;   // tiles of this cluster
     volatile int* abort = &bars->abort;
-    MLA_PROF(long long wacc[18] = {0};)
+    MLA_PROF(long long wacc[20] = {0};)
     MLA_PROF(const long long t_kernel0 = clock64();)
 
     if (threadIdx.x == 0) {
@@ -310,12 +310,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     const uint32_t base = smem_slots + sl * kSlotBytes;
                     const uint32_t p_tmem = tmem + kTmemS + sb * NK;
                     MLA_PROF(const long long tpv = clock64();)
-                    for (int k = 0; k < NK / 16; ++k) {
-                        // B = V [16 keys x 256 latent], MN-major, 128B swizzle:
-                        // LBO = stride between 64-dim chunks, SBO = stride between 8-key groups.
-                        const uint64_t bd = smem_desc(base + k * 16 * 128, kChunkBytes, 1024, 2);
-                        mma_ts(tmem + kTmemO, p_tmem + k * 8, bd, idesc_o, (first && k == 0) ? 0u : 1u);
-                    }
+                    // B = V [16 keys x 256 latent], MN-major, 128B swizzle:
+                    // LBO = stride between 64-dim chunks, SBO = stride between 8-key groups.
+                    const uint64_t vd0 = smem_desc(base, kChunkBytes, 1024, 2);
+#pragma unroll
+                    for (int k = 0; k < NK / 16; ++k)
+                        mma_ts(tmem + kTmemO, p_tmem + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4), idesc_o,
+                               (first && k == 0) ? 0u : 1u);
                     mma_commit(&bars->bf_empty[sl]);
                     mma_commit(&bars->o_done[sb]);
                     MLA_PROF(wacc[16] += clock64() - tpv;)
@@ -337,10 +338,21 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     const uint32_t base = smem_slots + sl * kSlotBytes;
                     const int sb = int(i % kSBufs);
                     MLA_PROF(const long long tsi = clock64();)
-                    for (int k = 0; k < dims / 16; ++k) {
-                        // B = K [32 keys x 16 dims], K-major, 128B swizzle: chunk k/4, +32 B per k-step.
-                        const uint64_t bd = smem_desc(base + (k >> 2) * kChunkBytes + (k & 3) * 32, 16, 1024, 2);
-                        mma_ts(tmem + kTmemS + sb * NK, tmem + kTmemQ + k * 8, bd, idesc_s, k > 0 ? 1u : 0u);
+                    // B = K [32 keys x 16 dims], K-major, 128B swizzle: chunk k/4, +32 B per
+                    // k-step. One descriptor per tile; each k-step adds a compile-time offset
+                    // to its start-address field (16-byte units), so the issuing thread does
+                    // one add per MMA.
+                    const uint64_t bd0 = smem_desc(base, 16, 1024, 2);
+                    const uint32_t d_s = tmem + kTmemS + sb * NK;
+#pragma unroll
+                    for (int k = 0; k < kHalf / 16; ++k)
+                        mma_ts(d_s, tmem + kTmemQ + k * 8,
+                               bd0 + uint64_t(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4), idesc_s, k > 0 ? 1u : 0u);
+                    if (rank == 1) {
+#pragma unroll
+                        for (int k = kHalf / 16; k < (kHalf + kRope) / 16; ++k)
+                            mma_ts(d_s, tmem + kTmemQ + k * 8,
+                                   bd0 + uint64_t(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4), idesc_s, 1u);
                     }
                     mma_commit(&bars->s_full[sb]);
                     MLA_PROF(wacc[17] += clock64() - tsi;)
@@ -499,6 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     l_run *= alpha;
                     m_run = mt;
                 }
+                MLA_PROF(wacc[18] += clock64() - tph;)
                 const float mc = m_run * c;
                 uint32_t pk[NK / 2];
                 float ls = 0.f;
@@ -516,8 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 }
                 l_run += ls;
                 __syncwarp();
+                MLA_PROF(const long long tst = clock64();)
                 tmem_st16(tmem + lane_off + kTmemS + sb * NK, pk);
                 tmem_st_wait();
+                MLA_PROF(wacc[19] += clock64() - tst;)
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
                 MLA_PROF(wacc[12] += clock64() - tph;)
@@ -634,6 +649,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             for (int k = 0; k < 15; ++k)
                 if (wacc[k]) trace_put(p, 8 + k, wacc[k] / 1000);
         if (threadIdx.x == 0) trace_put(p, 23, (clock64() - t_kernel0) / 1000);
+        if (warp == 4 && lane == 0) {
+            trace_put(p, 26, wacc[18] / 1000);
+            trace_put(p, 27, wacc[19] / 1000);
+        }
         if (warp == 1 && lane == 0) {
             trace_put(p, 24, wacc[16] / 1000);
             trace_put(p, 25, wacc[17] / 1000);
@@ -859,9 +878,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                 const volatile int* t = trace_host + b * 32;
                 fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d | kcyc total %d "
                         "stg_empty %d bf_empty(p) %d p_full %d q_ready %d bf_full %d s_full %d x_full %d o_resc %d "
-                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d pv_issue %d s_issue %d\n",
+                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d pv_issue %d s_issue %d | cmp_pre %d p_store %d\n",
                         (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[23], t[8], t[9], t[10], t[11], t[12],
-                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25]);
+                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25], t[26], t[27]);
             }
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);
