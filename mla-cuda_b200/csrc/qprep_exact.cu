@@ -75,16 +75,28 @@ __global__ void __launch_bounds__(256) lat_norm_kernel(
     T* __restrict__ q_lat, int64_t M, int64_t q_lora, acc_t<T> eps)
 {
     using Acc = acc_t<T>;
+    constexpr int kKeep = 8;            // values kept in registers per thread (q_lora <= 2048)
     const int64_t m = blockIdx.x;
     auto val = [&](int64_t n) {
         Acc v = Acc(0);
         for (int z = 0; z < splits; ++z) v += P1[(int64_t(z) * M + m) * q_lora + n];
         return v;
     };
+    const bool keep = q_lora <= int64_t(kKeep) * blockDim.x;
+    Acc kept[kKeep];
     Acc ss = Acc(0);
-    for (int64_t n = threadIdx.x; n < q_lora; n += blockDim.x) {
-        const Acc v = val(n);
-        ss = fma(v, v, ss);
+    if (keep) {   // one pass over the partials
+#pragma unroll
+        for (int e = 0; e < kKeep; ++e) {
+            const int64_t n = threadIdx.x + int64_t(e) * blockDim.x;
+            kept[e] = (n < q_lora) ? val(n) : Acc(0);
+            ss = fma(kept[e], kept[e], ss);
+        }
+    } else {
+        for (int64_t n = threadIdx.x; n < q_lora; n += blockDim.x) {
+            const Acc v = val(n);
+            ss = fma(v, v, ss);
+        }
     }
     __shared__ Acc red[32];
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
@@ -97,8 +109,16 @@ __global__ void __launch_bounds__(256) lat_norm_kernel(
     }
     __syncthreads();
     const Acc inv_rms = red[0];
-    for (int64_t n = threadIdx.x; n < q_lora; n += blockDim.x)
-        q_lat[m * q_lora + n] = cvt<T>(val(n) * inv_rms * cvt<Acc>(gain[n]));
+    if (keep) {
+#pragma unroll
+        for (int e = 0; e < kKeep; ++e) {
+            const int64_t n = threadIdx.x + int64_t(e) * blockDim.x;
+            if (n < q_lora) q_lat[m * q_lora + n] = cvt<T>(kept[e] * inv_rms * cvt<Acc>(gain[n]));
+        }
+    } else {
+        for (int64_t n = threadIdx.x; n < q_lora; n += blockDim.x)
+            q_lat[m * q_lora + n] = cvt<T>(val(n) * inv_rms * cvt<Acc>(gain[n]));
+    }
 }
 
 // 2b: reduce the 2a2 partials of every head into q_nope (acc dtype, the left
@@ -108,11 +128,27 @@ __global__ void __launch_bounds__(256) lat_norm_kernel(
 template <typename T>
 struct RopeTable { acc_t<T> inv_freq[kMaxRopePairs]; };
 
+// cos / sin of every (query index, pair): cs[s][j] = {cos, sin}(pos[s] * inv_freq[j]),
+// narrowed to the storage dtype as apply_rope does (exhaustive_benchmark_suite.py:222-223).
+template <typename T>
+__global__ void __launch_bounds__(256) rope_table_kernel(const int64_t* __restrict__ positions, int64_t sq,
+                                                         int64_t pairs, RopeTable<T> tab, acc_t<T>* __restrict__ cs)
+{
+    using Acc = acc_t<T>;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < sq * pairs;
+         i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t s = i / pairs, j = i % pairs;
+        const Acc ang = Acc(positions[s]) * tab.inv_freq[j];
+        cs[2 * i] = cvt<Acc>(cvt<T>(cos(ang)));
+        cs[2 * i + 1] = cvt<Acc>(cvt<T>(sin(ang)));
+    }
+}
+
 template <typename T, typename NopeT = acc_t<T>>
 __global__ void __launch_bounds__(256) rope_gather_kernel(
     const acc_t<T>* __restrict__ P2, int splits, const int64_t* __restrict__ positions,
     NopeT* __restrict__ q_nope, T* __restrict__ q_rope,
-    int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, RopeTable<T> tab)
+    int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, const acc_t<T>* __restrict__ cs)
 {
     using Acc = acc_t<T>;
     const int64_t qk = nope + rope;
@@ -136,11 +172,8 @@ __global__ void __launch_bounds__(256) rope_gather_kernel(
         } else {
             const int64_t j = e - nope;
             const Acc ev = sum(col), od = sum(col + 1);
-            const Acc ang = Acc(positions[m % sq]) * tab.inv_freq[j];
-            // cos/sin are narrowed to the storage dtype before use, as apply_rope does
-            // (exhaustive_benchmark_suite.py:222-223); a no-op for fp32/fp64.
-            const Acc c = cvt<Acc>(cvt<T>(cos(ang)));
-            const Acc s = cvt<Acc>(cvt<T>(sin(ang)));
+            const Acc* t = cs + 2 * ((m % sq) * (rope / 2) + j);
+            const Acc c = t[0], s = t[1];
             q_rope[mh * rope + 2 * j] = cvt<T>(ev * c - od * s);
             q_rope[mh * rope + 2 * j + 1] = cvt<T>(ev * s + od * c);
         }
@@ -193,7 +226,7 @@ struct QPlan {
     int64_t bm, bn, bk;
     int split1, split2;
     int64_t chunk1, chunk2;
-    size_t off_p1, off_qlat, off_p2, off_qnope, total;
+    size_t off_p1, off_qlat, off_p2, off_qnope, off_cs, total;
 };
 
 // Split-K plan: enough CTAs for ~4 resident waves, each split a whole number of
@@ -228,6 +261,7 @@ QPlan make_plan(const QArgs& a) {
     p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(T), 256);
     p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(Acc), 256);
     p.off_qnope = off; off = align_up(off + size_t(M) * a.heads * a.nope * sizeof(Acc), 256);
+    p.off_cs = off;    off = align_up(off + size_t(a.sq) * (a.rope / 2 + 1) * 2 * sizeof(Acc), 256);
     p.total = off;
     return p;
 }
@@ -301,9 +335,13 @@ mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
         const int64_t cap = 16LL * sm_count();
         if (blocks > cap) blocks = cap;
         if (blocks < 1) blocks = 1;
+        Acc* cs = reinterpret_cast<Acc*>(ws + p.off_cs);
+        rope_table_kernel<T><<<unsigned(ceil_div(a.sq * (a.rope / 2), 256) > 0 ? ceil_div(a.sq * (a.rope / 2), 256) : 1), 256, 0, st>>>(a.positions, a.sq,
+                                                                                               a.rope / 2, tab, cs);
+        MLA_TRY(check_launch("q rope table"));
         rope_gather_kernel<T><<<unsigned(blocks), 256, 0, st>>>(
             P2, p.split2, a.positions, q_nope, static_cast<T*>(a.q_rope),
-            M, a.sq, a.heads, a.nope, a.rope, tab);
+            M, a.sq, a.heads, a.nope, a.rope, cs);
         MLA_TRY(check_launch("q rope (2b)"));
     }
     if (p.small) {
@@ -335,7 +373,7 @@ namespace {
 struct QTPlan {
     int split1, split2;
     int64_t chunk1, chunk2;
-    size_t off_err, off_p1, off_qlat, off_p2, off_qnope, total;
+    size_t off_err, off_p1, off_qlat, off_p2, off_qnope, off_cs, total;
 };
 
 int tc_split(int64_t tiles, int64_t K, int64_t bk, int waves, int64_t& chunk) {
@@ -365,6 +403,7 @@ QTPlan make_tplan(const QArgs& a) {
     p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(T), 256);
     p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(Acc), 256);
     p.off_qnope = off; off = align_up(off + size_t(M) * a.heads * a.nope * sizeof(Acc), 256);
+    p.off_cs = off;    off = align_up(off + size_t(a.sq) * (a.rope / 2 + 1) * 2 * sizeof(Acc), 256);
     p.total = off;
     return p;
 }
@@ -433,9 +472,13 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
         if (blocks < 1) blocks = 1;
         // q_nope in the storage dtype: the left operand of the 2c tensor-core GEMM,
         // whose operands share one dtype
+        Acc* cs = reinterpret_cast<Acc*>(ws + p.off_cs);
+        rope_table_kernel<T><<<unsigned(ceil_div(a.sq * (a.rope / 2), 256) > 0 ? ceil_div(a.sq * (a.rope / 2), 256) : 1), 256, 0, st>>>(a.positions, a.sq,
+                                                                                               a.rope / 2, tab, cs);
+        MLA_TRY(check_launch("q rope table"));
         rope_gather_kernel<T, T><<<unsigned(blocks), 256, 0, st>>>(P2, p.split2, a.positions, q_nope_t,
                                                                     static_cast<T*>(a.q_rope), M, a.sq, a.heads,
-                                                                    a.nope, a.rope, tab);
+                                                                    a.nope, a.rope, cs);
         MLA_TRY(check_launch("q rope (2b)"));
     }
     TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h]

@@ -37,7 +37,9 @@ template <typename T> constexpr uint32_t fmt() {
     return std::is_same<T, float>::value ? 2u : std::is_same<T, __half>::value ? 0u : 1u;
 }
 
-template <int BN> constexpr int stages() { return BN == 256 ? 4 : 6; }
+// BN = 128 keeps 3 stages (97 KB) so that two CTAs share an SM: a 192-CTA launch
+// then runs in one wave on 148 SMs instead of 1.3.
+template <int BN> constexpr int stages() { return BN == 256 ? 4 : 3; }
 template <typename T, int BN> constexpr int a_bytes() { return 128 * 128; }        // 128 rows x 128 B
 template <typename T, int BN> constexpr int b_bytes() { return BN * 128; }         // BN x BK elements
 template <typename T, int BN> constexpr size_t smem_bytes() {
