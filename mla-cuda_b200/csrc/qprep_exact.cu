@@ -290,12 +290,23 @@ mla_status_t launch_absorb(const typename Cfg::Acc* qn, const T* W, T* out, cons
 
 }  // namespace
 
+template <typename T> size_t qprep_tensor_workspace(const QArgs& a);
+template <typename T> mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3);
+
+// fp32 storage: the exact path runs the tensor-core pipeline with 3xTF32 GEMMs
+// (fp32-class products, fp32 accumulation) wherever the shapes allow TMA tiles.
 template <typename T>
-size_t qprep_exact_workspace(const QArgs& a) { return make_plan<T>(a).total; }
+bool exact_uses_3xtf32(const QArgs& a) { return std::is_same<T, float>::value && qprep_tensor_supported<T>(a); }
+
+template <typename T>
+size_t qprep_exact_workspace(const QArgs& a) {
+    return exact_uses_3xtf32<T>(a) ? qprep_tensor_workspace<T>(a) : make_plan<T>(a).total;
+}
 
 template <typename T>
 mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
     using Acc = acc_t<T>;
+    if (exact_uses_3xtf32<T>(a)) return qprep_tensor_impl<T>(a, st, true);
     const QPlan p = make_plan<T>(a);
     const int64_t M = a.batch * a.sq;
     const int64_t ncols = a.heads * (a.nope + a.rope);
@@ -425,7 +436,10 @@ template <typename T>
 size_t qprep_tensor_workspace(const QArgs& a) { return make_tplan<T>(a).total; }
 
 template <typename T>
-mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
+mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) { return qprep_tensor_impl<T>(a, st, false); }
+
+template <typename T>
+mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3) {
     using Acc = acc_t<T>;
     const QTPlan p = make_tplan<T>(a);
     const int64_t M = a.batch * a.sq;
@@ -443,8 +457,8 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
     g1.A = a.x; g1.a_dims[0] = a.hidden; g1.a_dims[1] = 1; g1.a_dims[2] = M; g1.a_ld[0] = a.hidden; g1.a_ld[1] = a.hidden;
     g1.B = a.W_q_a; g1.b_mn = true; g1.b_dims[0] = a.q_lora; g1.b_dims[1] = a.hidden; g1.b_dims[2] = 1;
     g1.b_ld[0] = a.q_lora; g1.b_ld[1] = a.q_lora * a.hidden;
-    g1.M = M; g1.N = a.q_lora; g1.K = a.hidden; g1.Z = p.split1; g1.split = true; g1.k_chunk = p.chunk1;
-    g1.C = P1; g1.c_is_t = false; g1.c_ldm = a.q_lora; g1.c_ldz = M * a.q_lora; g1.bn = 128; g1.err = err;
+    g1.M = M; g1.N = a.q_lora; g1.K = a.hidden; g1.Z = p.split1; g1.spb = p.split1; g1.k_chunk = p.chunk1;
+    g1.C = P1; g1.c_is_t = false; g1.c_ldm = a.q_lora; g1.c_ldz = M * a.q_lora; g1.bn = 128; g1.err = err; g1.split3 = split3;
     MLA_TRY(tc_gemm<T>(g1, st));
 
     lat_norm_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, p.split1, static_cast<const T*>(a.q_norm_w), q_lat, M,
@@ -455,8 +469,8 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
     g2.A = q_lat; g2.a_dims[0] = a.q_lora; g2.a_dims[1] = 1; g2.a_dims[2] = M; g2.a_ld[0] = a.q_lora; g2.a_ld[1] = a.q_lora;
     g2.B = a.W_q_b; g2.b_mn = true; g2.b_dims[0] = ncols; g2.b_dims[1] = a.q_lora; g2.b_dims[2] = 1;
     g2.b_ld[0] = ncols; g2.b_ld[1] = ncols * a.q_lora;
-    g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = p.split2; g2.split = true; g2.k_chunk = p.chunk2;
-    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err;
+    g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = p.split2; g2.spb = p.split2; g2.k_chunk = p.chunk2;
+    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err; g2.split3 = split3;
     MLA_TRY(tc_gemm<T>(g2, st));
 
     RopeTable<T> tab{};
@@ -486,16 +500,17 @@ mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st) {
     g3.a_ld[0] = a.nope; g3.a_ld[1] = a.heads * a.nope;
     g3.B = a.W_uk; g3.b_mn = true; g3.b_dims[0] = a.kv_rank; g3.b_dims[1] = a.nope; g3.b_dims[2] = a.heads;
     g3.b_ld[0] = a.kv_rank; g3.b_ld[1] = a.nope * a.kv_rank;
-    g3.M = M; g3.N = a.kv_rank; g3.K = a.nope; g3.Z = int(a.heads); g3.split = false; g3.k_chunk = a.nope;
+    g3.M = M; g3.N = a.kv_rank; g3.K = a.nope; g3.Z = int(a.heads); g3.spb = 1; g3.k_chunk = a.nope;
     g3.C = a.q_absorbed; g3.c_is_t = true; g3.c_ldm = a.heads * a.kv_rank; g3.c_ldz = a.kv_rank;
-    g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err;
+    g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err; g3.split3 = split3;
     return tc_gemm<T>(g3, st);
 }
 
 #define MLA_QT(T) \
     template bool qprep_tensor_supported<T>(const QArgs&); \
     template size_t qprep_tensor_workspace<T>(const QArgs&); \
-    template mla_status_t qprep_tensor<T>(const QArgs&, cudaStream_t);
+    template mla_status_t qprep_tensor<T>(const QArgs&, cudaStream_t); \
+    template mla_status_t qprep_tensor_impl<T>(const QArgs&, cudaStream_t, bool);
 MLA_QT(float)
 MLA_QT(double)
 MLA_QT(__half)

@@ -901,7 +901,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         g.a_ld[0] = kRank; g.a_ld[1] = int64_t(kHeads) * kRank;
         g.B = a.W_uv; g.b_mn = false; g.b_dims[0] = kRank; g.b_dims[1] = a.v_dim; g.b_dims[2] = kHeads;
         g.b_ld[0] = kRank; g.b_ld[1] = a.v_dim * kRank;
-        g.M = pl.groups; g.N = a.v_dim; g.K = kRank; g.Z = kHeads; g.split = false; g.k_chunk = kRank;
+        g.M = pl.groups; g.N = a.v_dim; g.K = kRank; g.Z = kHeads; g.spb = 1; g.k_chunk = kRank;
         g.C = a.out; g.c_is_t = true; g.c_ldm = int64_t(kHeads) * a.v_dim; g.c_ldz = a.v_dim;
         g.bn = a.v_dim % 256 == 0 ? 256 : 128; g.err = p.err;
         return tc_gemm<T>(g, st);

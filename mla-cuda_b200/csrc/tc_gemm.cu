@@ -1,15 +1,14 @@
 // Tensor-core GEMM (tcgen05 + TMA) for the dense stages of the MLA forward.
 //
-// One CTA computes a 128 x BN output tile of one slice / batch z: warp 0 issues
+// One CTA computes a 128 x BN output tile of one launch index z: warp 0 issues
 // TMA loads of 128B-swizzled A and B blocks into a ring of stages, warp 1 (one
 // thread) issues the MMAs (M = 128, N = BN, K = 8 tf32 or 16 bf16/fp16 per
 // instruction) into a TMEM accumulator, warps 2-5 read the accumulator back
-// (one TMEM lane = one output row per thread) and store it. The weights of
-// these stages are streamed exactly once per 128-row block of activations, so
-// at decode batch sizes the kernel is bound by HBM bandwidth on the weights.
-//
-// fp32 operands run as kind::tf32 (10-bit mantissa, fp32 accumulation); this is
-// used only by the tensor-core precision of the MLA entry points.
+// (one TMEM lane = one output row per thread) and store it. With split3 (3xTF32,
+// fp32 operands) warps 2-5 first split every landed stage into tf32 heads (in
+// place) and fp32 remainders, and the MMA thread issues three MMAs per k-step.
+// At decode batch sizes the projections are bound by HBM bandwidth on their
+// weights, which every tile streams once.
 #include "tc_gemm.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -23,44 +22,53 @@ namespace tcg {
 using namespace sm100;
 
 constexpr int kThreads = 192;
+constexpr int kGroup = 2;   // 3xTF32: K blocks summed into one TMEM accumulator before it is drained
 enum : int { ERR_TIMEOUT_BASE = 200 };
 
 struct Run {
     int64_t M, N, K, k_chunk;
-    int Z, split, b_mn, c_is_t;
+    int Z, spb, b_mn, c_is_t, c_accum, a_batch_outer;
     void* C; int64_t c_ldm, c_ldz;
     int* err;
-    int dbg;
 };
 
 template <typename T> constexpr uint32_t fmt() {
     return std::is_same<T, float>::value ? 2u : std::is_same<T, __half>::value ? 0u : 1u;
 }
 
-// BN = 128 keeps 3 stages (97 KB) so that two CTAs share an SM: a 192-CTA launch
-// then runs in one wave on 148 SMs instead of 1.3.
-template <int BN> constexpr int stages() { return BN == 256 ? 4 : 3; }
-template <typename T, int BN> constexpr int a_bytes() { return 128 * 128; }        // 128 rows x 128 B
-template <typename T, int BN> constexpr int b_bytes() { return BN * 128; }         // BN x BK elements
-template <typename T, int BN> constexpr size_t smem_bytes() {
-    return 1024 + size_t(stages<BN>()) * (a_bytes<T, BN>() + b_bytes<T, BN>()) + 256;
+// Stage counts: BN = 128 keeps 3 stages (97 KB) so two CTAs share an SM (a
+// 192-CTA launch runs in one wave on 148 SMs); 3xTF32 stages also hold the
+// remainders, so they are twice as large.
+template <int BN, bool S3> constexpr int stages() { return S3 ? (BN == 256 ? 2 : 3) : (BN == 256 ? 4 : 3); }
+constexpr int a_bytes() { return 128 * 128; }                     // 128 rows x 128 B
+template <int BN> constexpr int b_bytes() { return BN * 128; }   // BN x one 128-byte K block
+template <int BN, bool S3> constexpr size_t smem_bytes() {
+    return 1024 + size_t(stages<BN, S3>()) * (a_bytes() + b_bytes<BN>()) * (S3 ? 2 : 1) + 512;
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool S3>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Run r)
 {
-    constexpr int S = stages<BN>();
+    constexpr int S = stages<BN, S3>();
     constexpr int BK = tc_gemm_bk<T>();             // elements per 128-byte row
     constexpr int kInstK = 32 / int(sizeof(T));      // K per MMA instruction (32 bytes)
+    constexpr int kStage = a_bytes() + b_bytes<BN>();
+    // 3xTF32: two accumulators of BN columns (ping-pong over groups of kGroup K blocks)
+    // and a running sum at 2*BN
+    constexpr uint32_t kTmemCols = S3 ? 512u : uint32_t(BN);
+    static_assert(!S3 || BN == 128, "3xTF32 uses 128-column tiles");
+    static_assert(!S3 || std::is_same<T, float>::value, "3xTF32 needs fp32 operands");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* As = smem;
-    unsigned char* Bs = smem + S * a_bytes<T, BN>();
-    uint64_t* full = reinterpret_cast<uint64_t*>(Bs + S * b_bytes<T, BN>());
+    // stage s: [A | B] at smem + s*kStage; 3xTF32 remainders at lo + s*kStage
+    unsigned char* lo = smem + S * kStage;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStage * (S3 ? 2 : 1));
     uint64_t* empty = full + S;
-    uint64_t* acc_full = empty + S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* split_done = empty + S;
+    uint64_t* acc_full = split_done + S;          // [2]: accumulator buffer ready (3xTF32 uses both)
+    uint64_t* acc_empty = acc_full + 2;           // [2]: 3xTF32 accumulator drained into the sum
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     volatile int* abort = abort_flag;
 
@@ -68,24 +76,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     const int64_t n0 = int64_t(blockIdx.x) * BN;
     const int64_t m0 = int64_t(blockIdx.y) * 128;
     const int z = blockIdx.z;
-    int64_t kb = 0, ke = r.K;
-    if (r.split) {
-        kb = int64_t(z) * r.k_chunk;
-        ke = min(r.K, kb + r.k_chunk);
-    }
+    const int ya = z / r.spb;                       // batch
+    const int64_t kb = int64_t(z % r.spb) * r.k_chunk;
+    const int64_t ke = min(r.K, kb + r.k_chunk);
     const int64_t nkb = ke > kb ? (ke - kb + BK - 1) / BK : 0;
-    const int ya = r.split ? 0 : z;      // batch coordinate of A and B
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
+            mbar_init(&split_done[i], 128);
         }
-        mbar_init(acc_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, BN);
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -98,9 +107,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
             const int s = int(i % S);
             if (!mbar_wait(&empty[s], uint32_t(((i / S) & 1) ^ 1), abort, r.err, ERR_TIMEOUT_BASE + 1)) break;
             const int32_t k = int32_t(kb + i * BK);
-            mbar_arrive_expect_tx(&full[s], uint32_t(a_bytes<T, BN>() + b_bytes<T, BN>()));
-            tma_load_3d(As + s * a_bytes<T, BN>(), &tmA, &full[s], k, ya, int32_t(m0));
-            unsigned char* bdst = Bs + s * b_bytes<T, BN>();
+            unsigned char* st = smem + s * kStage;
+            mbar_arrive_expect_tx(&full[s], uint32_t(kStage));
+            if (r.a_batch_outer) tma_load_3d(st, &tmA, &full[s], k, int32_t(m0), ya);
+            else tma_load_3d(st, &tmA, &full[s], k, ya, int32_t(m0));
+            unsigned char* bdst = st + a_bytes();
             if (r.b_mn) {
                 for (int g = 0; g < BN / BK; ++g)   // BK-wide column groups of N, BK rows of K each
                     tma_load_3d(bdst + g * (BK * 128), &tmB, &full[s], int32_t(n0 + g * BK), k, ya);
@@ -113,70 +124,160 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
         bool ok = true;
         for (int64_t i = 0; i < nkb; ++i) {
             const int s = int(i % S);
-            if (!mbar_wait(&full[s], uint32_t((i / S) & 1), abort, r.err, ERR_TIMEOUT_BASE + 2)) { ok = false; break; }
+            uint64_t* ready = S3 ? &split_done[s] : &full[s];
+            if (!mbar_wait(ready, uint32_t((i / S) & 1), abort, r.err, ERR_TIMEOUT_BASE + 2)) { ok = false; break; }
+            uint32_t d = tmem;
+            bool fresh = i == 0;
+            if constexpr (S3) {
+                const int64_t gi = i / kGroup;
+                d = tmem + uint32_t(gi & 1) * BN;
+                fresh = i % kGroup == 0;
+                if (fresh && !mbar_wait(&acc_empty[gi & 1], uint32_t(((gi >> 1) & 1) ^ 1), abort, r.err,
+                                        ERR_TIMEOUT_BASE + 5)) { ok = false; break; }
+            }
             tc_fence_after();
-            if (r.dbg && i == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-                printf("[gemm dbg] nkb %lld kb %lld A0 %08x %08x B0 %08x %08x\n", (long long)nkb, (long long)kb,
-                       reinterpret_cast<const uint32_t*>(As)[0], reinterpret_cast<const uint32_t*>(As)[1],
-                       reinterpret_cast<const uint32_t*>(Bs)[0], reinterpret_cast<const uint32_t*>(Bs)[1]);
-            const uint32_t a0 = smem_u32(As + s * a_bytes<T, BN>());
-            const uint32_t b0 = smem_u32(Bs + s * b_bytes<T, BN>());
+            const uint32_t a0 = smem_u32(smem + s * kStage);
+            const uint32_t b0 = a0 + a_bytes();
+            // B MN-major: column groups BK*128 bytes apart (LBO), K-row groups SBO apart:
+            // 8 rows / 1024 B with the 16-byte swizzle atoms of 16-bit types; for 32-bit
+            // (tf32) operands the MN-major layout uses 32-byte atoms, 4-row groups (512 B).
+            constexpr bool kA32 = sizeof(T) == 4;
+            const uint64_t ad0 = smem_desc(a0, 16, 1024, 2);
+            const uint64_t bd0 = r.b_mn ? smem_desc(b0, BK * 128, kA32 ? 512 : 1024, kA32 ? 1 : 2)
+                                        : smem_desc(b0, 16, 1024, 2);
+            const uint64_t lo_off = uint64_t((S * kStage) >> 4);   // remainder copy, same layout
+#pragma unroll
             for (int kk = 0; kk < BK / kInstK; ++kk) {
-                const uint64_t ad = smem_desc(a0 + kk * 32, 16, 1024, 2);
-                // B MN-major: column groups BK*128 bytes apart (LBO), K-row groups SBO apart:
-                // 8 rows / 1024 B with the 16-byte swizzle atoms of 16-bit types; for 32-bit
-                // (tf32) operands the MN-major layout uses 32-byte atoms, 4-row groups (512 B).
-                constexpr bool kA32 = sizeof(T) == 4;
-                const uint64_t bd = r.b_mn ? smem_desc(b0 + kk * (kInstK * 128), BK * 128, kA32 ? 512 : 1024,
-                                                       kA32 ? 1 : 2)
-                                           : smem_desc(b0 + kk * 32, 16, 1024, 2);
-                if constexpr (std::is_same<T, float>::value) mma_ss_tf32(tmem, ad, bd, idesc, (i | kk) ? 1u : 0u);
-                else mma_ss(tmem, ad, bd, idesc, (i | kk) ? 1u : 0u);
+                const uint64_t ad = ad0 + uint64_t((kk * 32) >> 4);
+                const uint64_t bd = bd0 + uint64_t((r.b_mn ? kk * (kInstK * 128) : kk * 32) >> 4);
+                const uint32_t acc = (fresh && kk == 0) ? 0u : 1u;
+                if constexpr (std::is_same<T, float>::value) {
+                    if constexpr (S3) {   // small terms first
+                        mma_ss_tf32(d, ad, bd + lo_off, idesc, acc);     // hi * lo
+                        mma_ss_tf32(d, ad + lo_off, bd, idesc, 1u);      // lo * hi
+                        mma_ss_tf32(d, ad, bd, idesc, 1u);               // hi * hi
+                    } else {
+                        mma_ss_tf32(d, ad, bd, idesc, acc);
+                    }
+                } else {
+                    mma_ss(d, ad, bd, idesc, acc);
+                }
             }
             mma_commit(&empty[s]);
+            if constexpr (S3) {
+                if ((i + 1) % kGroup == 0 || i + 1 == nkb) mma_commit(&acc_full[(i / kGroup) & 1]);
+            }
         }
-        if (ok) mma_commit(acc_full);
+        if (ok && !S3) mma_commit(acc_full);
     } else if (warp >= 2) {
         const int q = warp & 3;                       // TMEM lane quadrant of this warp
         const int row = q * 32 + lane;
         const int64_t m = m0 + row;
         bool ok = true;
-        if (nkb > 0) {
-            ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort, r.err, ERR_TIMEOUT_BASE + 3));
-            tc_fence_after();
+        const uint32_t lane_off = uint32_t(q * 32) << 16;
+        uint32_t res = tmem;                          // accumulator the output is read from
+        if constexpr (S3) {
+            // split each landed stage: x = hi + lo with hi = x truncated to tf32 (kept in
+            // place) and lo = x - hi (exact in fp32; the MMA reads it as tf32 again).
+            // The tensor core's fp32 accumulation does not round to nearest, so its error
+            // grows with the number of MMAs summed into one accumulator: every kGroup K
+            // blocks the accumulator is drained into a running sum (fp32, round to
+            // nearest) kept in TMEM columns [2*BN, 3*BN).
+            const int t = threadIdx.x - 64;
+            const int64_t ngroups = (nkb + kGroup - 1) / kGroup;
+            auto harvest = [&](int64_t gi) -> bool {
+                if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[gi & 1], uint32_t((gi >> 1) & 1), abort, r.err,
+                                                       ERR_TIMEOUT_BASE + 6)))
+                    return false;
+                tc_fence_after();
+                const uint32_t src = tmem + lane_off + uint32_t(gi & 1) * BN;
+                const uint32_t sum = tmem + lane_off + 2u * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(src + c * 32, v);
+                    if (gi > 0) {
+                        uint32_t u[32];
+                        tmem_ld32(sum + c * 32, u);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) + __uint_as_float(u[e]));
+                    } else {
+                        tmem_ld_wait();
+                    }
+                    tmem_st32(sum + c * 32, v);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&acc_empty[gi & 1]);
+                return true;
+            };
+            for (int64_t i = 0; i < nkb && ok; ++i) {
+                const int s = int(i % S);
+                ok = __all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t((i / S) & 1), abort, r.err,
+                                                       ERR_TIMEOUT_BASE + 4));
+                if (!ok) break;
+                uint4* x = reinterpret_cast<uint4*>(smem + s * kStage);
+                uint4* y = reinterpret_cast<uint4*>(lo + s * kStage);
+#pragma unroll 4
+                for (int e = t; e < kStage / 16; e += 128) {
+                    uint4 v = x[e], h, l;
+                    h.x = v.x & 0xffffe000u; h.y = v.y & 0xffffe000u; h.z = v.z & 0xffffe000u; h.w = v.w & 0xffffe000u;
+                    l.x = __float_as_uint(__uint_as_float(v.x) - __uint_as_float(h.x));
+                    l.y = __float_as_uint(__uint_as_float(v.y) - __uint_as_float(h.y));
+                    l.z = __float_as_uint(__uint_as_float(v.z) - __uint_as_float(h.z));
+                    l.w = __float_as_uint(__uint_as_float(v.w) - __uint_as_float(h.w));
+                    x[e] = h;
+                    y[e] = l;
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&split_done[s]);
+                // drain the previous group once this group's last block is handed over,
+                // so the MMAs of this group overlap the drain
+                if (((i + 1) % kGroup == 0 || i + 1 == nkb) && i / kGroup >= 1) ok = harvest(i / kGroup - 1);
+            }
+            if (ok && ngroups > 0) ok = harvest(ngroups - 1);
+            res = tmem + 2u * BN;
+        } else {
+            if (ok && nkb > 0) {
+                ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort, r.err, ERR_TIMEOUT_BASE + 3));
+                tc_fence_after();
+            }
         }
         if (ok) {
-            const uint32_t lane_off = uint32_t(q * 32) << 16;
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 if (nkb > 0) {
-                    tmem_ld32(tmem + lane_off + c * 32, v);
+                    tmem_ld32(res + lane_off + c * 32, v);
                     tmem_ld_wait();
                 } else {
                     for (int e = 0; e < 32; ++e) v[e] = 0u;
                 }
                 const int64_t n = n0 + c * 32;
-                if (r.dbg && c == 0 && row == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-                    printf("[gemm dbg] acc row0 %f %f  M %lld N %lld ldm %lld\n", __uint_as_float(v[0]),
-                           __uint_as_float(v[1]), (long long)r.M, (long long)r.N, (long long)r.c_ldm);
                 if (m >= r.M || n >= r.N) continue;
                 const int64_t off = m * r.c_ldm + int64_t(z) * r.c_ldz + n;
                 if (!r.c_is_t || std::is_same<T, float>::value) {
                     float4* d = reinterpret_cast<float4*>(static_cast<float*>(r.C) + off);
-                    for (int e = 0; e < 8; ++e)
-                        d[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
-                                           __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                    for (int e = 0; e < 8; ++e) {
+                        float4 o = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                               __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                        if (r.c_accum) {
+                            const float4 prev = d[e];
+                            o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
+                        }
+                        d[e] = o;
+                    }
                 } else {
                     uint4* d = reinterpret_cast<uint4*>(static_cast<T*>(r.C) + off);
                     for (int e = 0; e < 4; ++e) {
                         uint32_t w[4];
                         for (int h = 0; h < 4; ++h) {
-                            const float lo = __uint_as_float(v[8 * e + 2 * h]), hi = __uint_as_float(v[8 * e + 2 * h + 1]);
+                            const float lo_ = __uint_as_float(v[8 * e + 2 * h]), hi = __uint_as_float(v[8 * e + 2 * h + 1]);
                             if constexpr (std::is_same<T, __half>::value) {
-                                __half2 h2 = __floats2half2_rn(lo, hi);
+                                __half2 h2 = __floats2half2_rn(lo_, hi);
                                 w[h] = *reinterpret_cast<uint32_t*>(&h2);
                             } else {
-                                w[h] = pack_bf16(lo, hi);
+                                w[h] = pack_bf16(lo_, hi);
                             }
                         }
                         d[e] = make_uint4(w[0], w[1], w[2], w[3]);
@@ -193,24 +294,24 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     }
     tc_fence_after();
     __syncwarp();
-    if (warp == 1) tmem_dealloc(tmem, BN);
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
-template <typename T, int BN>
+template <typename T, int BN, bool S3>
 mla_status_t launch(const TcGemm& g, cudaStream_t st) {
     constexpr int BK = tc_gemm_bk<T>();
     CUtensorMap ta, tb;
-    const uint32_t abox[3] = {uint32_t(BK), 1u, 128u};
+    const uint32_t abox[3] = {uint32_t(BK), g.a_batch_outer ? 128u : 1u, g.a_batch_outer ? 1u : 128u};
     const uint32_t bbox_mn[3] = {uint32_t(BK), uint32_t(BK), 1u};
     const uint32_t bbox_k[3] = {uint32_t(BK), uint32_t(BN), 1u};
     if (!make_map_3d<T>(&ta, g.A, g.a_dims, g.a_ld, abox, true) ||
         !make_map_3d<T>(&tb, g.B, g.b_dims, g.b_ld, g.b_mn ? bbox_mn : bbox_k, true,
                         /*atom32=*/g.b_mn && sizeof(T) == 4))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
-    Run r{g.M, g.N, g.K, g.k_chunk, g.Z, g.split ? 1 : 0, g.b_mn ? 1 : 0, g.c_is_t ? 1 : 0, g.C, g.c_ldm, g.c_ldz,
-          g.err, getenv("MLA_GEMM_DEBUG") ? 1 : 0};
-    auto kern = tc_gemm_kernel<T, BN>;
-    const size_t smem = smem_bytes<T, BN>();
+    Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
+          g.c_is_t ? 1 : 0, g.c_accum ? 1 : 0, g.a_batch_outer ? 1 : 0, g.C, g.c_ldm, g.c_ldz, g.err};
+    auto kern = tc_gemm_kernel<T, BN, S3>;
+    const size_t smem = smem_bytes<BN, S3>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     dim3 grid(unsigned(ceil_div(g.N, BN)), unsigned(ceil_div(g.M, 128)), unsigned(g.Z));
     kern<<<grid, kThreads, smem, st>>>(ta, tb, r);
@@ -226,8 +327,14 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
     } else {
         if (g.N % 32 != 0 || g.c_ldm % 8 != 0 || g.c_ldz % 8 != 0)
             return set_error(MLA_ERR_UNSUPPORTED, "MLA: tensor-core GEMM needs N, ldm, ldz multiples of 32/8");
-        if (g.bn == 256) return tcg::launch<T, 256>(g, st);
-        return tcg::launch<T, 128>(g, st);
+        if (g.Z <= 0 || g.M <= 0) return MLA_OK;
+        if constexpr (std::is_same<T, float>::value) {
+            if (g.split3) return tcg::launch<T, 128, true>(g, st);
+        } else {
+            if (g.split3) return set_error(MLA_ERR_UNSUPPORTED, "MLA: 3xTF32 needs fp32 operands");
+        }
+        if (g.bn == 256) return tcg::launch<T, 256, false>(g, st);
+        return tcg::launch<T, 128, false>(g, st);
     }
 }
 
