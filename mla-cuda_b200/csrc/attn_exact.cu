@@ -17,8 +17,17 @@
 // before P @ c_kv runs, each probability is a single exp(S - M) with no
 // rescaling of partial sums. Key splits of the P @ c_kv product are combined
 // by plain sums in the last launch, which keeps the result deterministic.
+//
+// fp32 storage runs the same four steps with the three contractions on the
+// tensor cores in 3xTF32 (fp32-class products, fp32 accumulation drained into a
+// round-to-nearest sum every 64 K elements):
+//   S    = q_absorbed @ c_kv^T, then S += q_rope @ pe^T      (per batch)
+//   rows P = exp(S/scale - M) in place, l = sum P, M = max    (one warp per row)
+//   ctx  = P @ c_kv split over keys, reduced and divided by l (per batch)
+//   out  = ctx[:, h] @ W_uv[h]^T                               (per head)
 #include "qprep.cuh"
 #include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
 
 #include <type_traits>
 
@@ -349,12 +358,182 @@ template mla_status_t attn_out_normalized<float>(const AArgs&, const float*, cud
 template mla_status_t attn_out_normalized<__half>(const AArgs&, const float*, cudaStream_t);
 template mla_status_t attn_out_normalized<__nv_bfloat16>(const AArgs&, const float*, cudaStream_t);
 
+// ------------------------------------------------------------ fp32 on the tensor cores (3xTF32)
+namespace {
+
+// One warp per row: scaled, causally masked scores -> unnormalised probabilities
+// in place, with the row max and the sum of the probabilities.
+__global__ void __launch_bounds__(256) softmax_rows_kernel(
+    float* __restrict__ S, float* __restrict__ row_max, float* __restrict__ row_sum,
+    int64_t rows_total, int64_t ld, int64_t sk, int64_t sq, int64_t heads, float scale, int causal)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t g = blockIdx.x * 8LL + warp; g < rows_total; g += int64_t(gridDim.x) * 8) {
+        float* srow = S + g * ld;
+        const int64_t q = (g / heads) % sq;
+        const int64_t last_key = causal ? (sk - sq + q) : (sk - 1);
+        const int64_t n = last_key + 1 < sk ? last_key + 1 : sk;     // keys that are visible
+        float mx = neg_inf<float>();
+        for (int64_t k = lane; k < n; k += 32) {
+            const float v = srow[k] / scale;
+            mx = v > mx ? v : mx;
+        }
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const bool none = !(mx > neg_inf<float>());                    // every key masked
+        float l = 0.f;
+        for (int64_t k = lane; k < sk; k += 32) {
+            const float pk = (k < n && !none) ? fexp(srow[k] / scale - mx) : 0.f;
+            srow[k] = pk;
+            l += pk;
+        }
+        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (lane == 0) {
+            row_max[g] = mx;
+            row_sum[g] = l;
+        }
+    }
+}
+
+// ctx[g, :] = sum over key slices of the partial products / l[g]; lse[g] = M + log l.
+// parts: [batch][slices][rows_b][R]; ctx: [rows_total][R] with g = b * rows_b + row.
+__global__ void __launch_bounds__(256) ctx_reduce_kernel(
+    const float* __restrict__ parts, const float* __restrict__ row_max, const float* __restrict__ row_sum,
+    float* __restrict__ ctx, float* __restrict__ lse, int64_t rows_b, int64_t rows_total, int64_t R, int slices)
+{
+    const int64_t total4 = rows_total * R / 4;
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total4; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t e = i * 4;
+        const int64_t g = e / R, r = e % R;
+        const int64_t b = g / rows_b, row = g % rows_b;
+        const float l = row_sum[g];
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int z = 0; z < slices; ++z) {
+            const float4 v = *reinterpret_cast<const float4*>(parts + ((b * slices + z) * rows_b + row) * R + r);
+            acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+        *reinterpret_cast<float4*>(ctx + e) = acc;
+        if (lse && r == 0) lse[g] = row_max[g] + logf(l);
+    }
+}
+
+struct T3Plan {
+    int64_t rows_b, rows_total, ld, chunk;
+    int slices;
+    size_t off_err, off_S, off_max, off_sum, off_parts, off_ctx, total;
+};
+
+T3Plan make_t3plan(const AArgs& a) {
+    T3Plan p{};
+    p.rows_b = a.sq * a.heads;
+    p.rows_total = a.batch * p.rows_b;
+    p.ld = (a.sk + 31) / 32 * 32;
+    // key slices of P @ c_kv: fill about two waves of SMs, at least 8 K blocks each
+    const int64_t tiles = ceil_div(p.rows_b, 128) * ceil_div(a.kv_rank, 128) * a.batch;
+    const int64_t kblocks = ceil_div(a.sk, 32);
+    int64_t s = (2LL * sm_count()) / (tiles > 0 ? tiles : 1);
+    if (s > kblocks / 8) s = kblocks / 8;
+    if (s > 65535 / (a.batch > 0 ? a.batch : 1)) s = 65535 / (a.batch > 0 ? a.batch : 1);
+    if (s < 1) s = 1;
+    const int64_t cb = ceil_div(kblocks, s);
+    p.chunk = cb * 32;
+    p.slices = int(ceil_div(kblocks, cb));
+    size_t off = 0;
+    p.off_err = off;   off = align_up(off + 256, 256);
+    p.off_S = off;     off = align_up(off + size_t(p.rows_total) * p.ld * sizeof(float), 256);
+    p.off_max = off;   off = align_up(off + size_t(p.rows_total) * sizeof(float), 256);
+    p.off_sum = off;   off = align_up(off + size_t(p.rows_total) * sizeof(float), 256);
+    p.off_parts = off; off = align_up(off + size_t(p.slices) * p.rows_total * a.kv_rank * sizeof(float), 256);
+    p.off_ctx = off;   off = align_up(off + size_t(p.rows_total) * a.kv_rank * sizeof(float), 256);
+    p.total = off;
+    return p;
+}
+
+// TMA needs 16-byte strides and the GEMM 32-column tiles of the latent.
+bool t3_supported(const AArgs& a) {
+    return a.kv_rank % 32 == 0 && a.rope % 4 == 0 && a.rope > 0 && a.sk > 0 && a.batch > 0 && a.sq > 0 &&
+           a.heads > 0 && a.batch * a.sq * a.heads * a.sk < (int64_t(1) << 31);
+}
+
+mla_status_t attn_exact_t3(const AArgs& a, cudaStream_t st) {
+    const T3Plan p = make_t3plan(a);
+    char* ws = static_cast<char*>(a.workspace);
+    int* err = reinterpret_cast<int*>(ws + p.off_err);
+    float* S = reinterpret_cast<float*>(ws + p.off_S);
+    float* rmax = reinterpret_cast<float*>(ws + p.off_max);
+    float* rsum = reinterpret_cast<float*>(ws + p.off_sum);
+    float* parts = reinterpret_cast<float*>(ws + p.off_parts);
+    float* ctx = reinterpret_cast<float*>(ws + p.off_ctx);
+    if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
+        return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
+
+    // S[b] = q_absorbed[b] [rows_b, R] @ c_kv[b]^T; keys past sk read as zeros (TMA
+    // fill) and land in the padding columns [sk, ld)
+    TcGemm g1{};
+    g1.A = a.q_absorbed; g1.a_dims[0] = a.kv_rank; g1.a_dims[1] = a.batch; g1.a_dims[2] = p.rows_b;
+    g1.a_ld[0] = p.rows_b * a.kv_rank; g1.a_ld[1] = a.kv_rank;
+    g1.B = a.c_kv; g1.b_mn = false; g1.b_dims[0] = a.kv_rank; g1.b_dims[1] = a.sk; g1.b_dims[2] = a.batch;
+    g1.b_ld[0] = a.kv_rank; g1.b_ld[1] = a.sk * a.kv_rank;
+    g1.M = p.rows_b; g1.N = p.ld; g1.K = a.kv_rank; g1.Z = int(a.batch); g1.spb = 1; g1.k_chunk = a.kv_rank;
+    g1.C = S; g1.c_ldm = p.ld; g1.c_ldz = p.rows_b * p.ld; g1.bn = 128; g1.split3 = true; g1.err = err;
+    MLA_TRY(tc_gemm<float>(g1, st));
+    TcGemm g2 = g1;   // S[b] += q_rope[b] @ pe[b]^T
+    g2.A = a.q_rope; g2.a_dims[0] = a.rope; g2.a_ld[0] = p.rows_b * a.rope; g2.a_ld[1] = a.rope;
+    g2.B = a.pe_cache; g2.b_dims[0] = a.rope; g2.b_ld[0] = a.rope; g2.b_ld[1] = a.sk * a.rope;
+    g2.K = a.rope; g2.k_chunk = a.rope; g2.c_accum = true;
+    MLA_TRY(tc_gemm<float>(g2, st));
+
+    {
+        int64_t blocks = ceil_div(p.rows_total, 8);
+        if (blocks > 16LL * sm_count()) blocks = 16LL * sm_count();
+        softmax_rows_kernel<<<unsigned(blocks), 256, 0, st>>>(S, rmax, rsum, p.rows_total, p.ld, a.sk, a.sq,
+                                                              a.heads, float(a.scale), a.causal);
+        MLA_TRY(check_launch("attention softmax rows"));
+    }
+
+    TcGemm g3{};      // parts[b][z] = P[b][:, keys of slice z] @ c_kv[b][keys of slice z, :]
+    g3.A = S; g3.a_dims[0] = a.sk; g3.a_dims[1] = a.batch; g3.a_dims[2] = p.rows_b;
+    g3.a_ld[0] = p.rows_b * p.ld; g3.a_ld[1] = p.ld;
+    g3.B = a.c_kv; g3.b_mn = true; g3.b_dims[0] = a.kv_rank; g3.b_dims[1] = a.sk; g3.b_dims[2] = a.batch;
+    g3.b_ld[0] = a.kv_rank; g3.b_ld[1] = a.sk * a.kv_rank;
+    g3.M = p.rows_b; g3.N = a.kv_rank; g3.K = a.sk; g3.Z = int(a.batch) * p.slices; g3.spb = p.slices;
+    g3.k_chunk = p.chunk;
+    g3.C = parts; g3.c_ldm = a.kv_rank; g3.c_ldz = p.rows_b * a.kv_rank; g3.bn = 128; g3.split3 = true; g3.err = err;
+    MLA_TRY(tc_gemm<float>(g3, st));
+
+    {
+        int64_t blocks = ceil_div(p.rows_total * a.kv_rank / 4, 256);
+        if (blocks > 32LL * sm_count()) blocks = 32LL * sm_count();
+        ctx_reduce_kernel<<<unsigned(blocks), 256, 0, st>>>(parts, rmax, rsum, ctx, a.lse, p.rows_b, p.rows_total,
+                                                            a.kv_rank, p.slices);
+        MLA_TRY(check_launch("attention context reduce"));
+    }
+    if (a.v_dim % 32 != 0) return attn_out_normalized<float>(a, ctx, st);
+    TcGemm g4{};      // out[:, h] = ctx[:, h] @ W_uv[h]^T
+    const int64_t groups = a.batch * a.sq;
+    g4.A = ctx; g4.a_dims[0] = a.kv_rank; g4.a_dims[1] = a.heads; g4.a_dims[2] = groups;
+    g4.a_ld[0] = a.kv_rank; g4.a_ld[1] = a.heads * a.kv_rank;
+    g4.B = a.W_uv; g4.b_mn = false; g4.b_dims[0] = a.kv_rank; g4.b_dims[1] = a.v_dim; g4.b_dims[2] = a.heads;
+    g4.b_ld[0] = a.kv_rank; g4.b_ld[1] = a.v_dim * a.kv_rank;
+    g4.M = groups; g4.N = a.v_dim; g4.K = a.kv_rank; g4.Z = int(a.heads); g4.spb = 1; g4.k_chunk = a.kv_rank;
+    g4.C = a.out; g4.c_is_t = true; g4.c_ldm = a.heads * a.v_dim; g4.c_ldz = a.v_dim; g4.bn = 128;
+    g4.split3 = true; g4.err = err;
+    return tc_gemm<float>(g4, st);
+}
+
+}  // namespace
+
 template <typename T>
-size_t attn_exact_workspace(const AArgs& a) { return make_plan<T>(a).total; }
+size_t attn_exact_workspace(const AArgs& a) {
+    if (std::is_same<T, float>::value && t3_supported(a)) return make_t3plan(a).total;
+    return make_plan<T>(a).total;
+}
 
 template <typename T>
 mla_status_t attn_exact(const AArgs& a, cudaStream_t st) {
     using Acc = acc_t<T>;
+    if (std::is_same<T, float>::value && t3_supported(a)) return attn_exact_t3(a, st);
     const APlan p = make_plan<T>(a);
     char* ws = static_cast<char*>(a.workspace);
     Acc* S = reinterpret_cast<Acc*>(ws + p.off_S);
