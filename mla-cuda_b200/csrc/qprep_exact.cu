@@ -180,6 +180,138 @@ __global__ void __launch_bounds__(256) rope_gather_kernel(
     }
 }
 
+// Vectorised 2a-norm for an fp32 accumulator: one block of 256 threads per row,
+// each thread owning up to kVec float4 pieces of the row, all split-K partial loads
+// of a piece issued together. Same sums, in the same order, as lat_norm_kernel.
+template <typename T>
+__global__ void __launch_bounds__(256) lat_norm_vec_kernel(
+    const float* __restrict__ P1, int splits, const T* __restrict__ gain,
+    T* __restrict__ q_lat, int64_t M, int64_t q_lora, float eps)
+{
+    constexpr int kVec = 2;                       // q_lora <= 2048
+    const int64_t m = blockIdx.x;
+    const int n4 = int(q_lora / 4);
+    float4 v[kVec];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < kVec; ++e) {
+        const int c = threadIdx.x + e * 256;
+        v[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c < n4) {
+            for (int z = 0; z < splits; ++z) {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(P1 + (int64_t(z) * M + m) * q_lora) + c);
+                v[e].x += t.x; v[e].y += t.y; v[e].z += t.z; v[e].w += t.w;
+            }
+        }
+        ss = fmaf(v[e].x, v[e].x, ss); ss = fmaf(v[e].y, v[e].y, ss);
+        ss = fmaf(v[e].z, v[e].z, ss); ss = fmaf(v[e].w, v[e].w, ss);
+    }
+    __shared__ float red[8];
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w];
+    const float inv_rms = 1.f / sqrtf(t / float(q_lora) + eps);
+#pragma unroll
+    for (int e = 0; e < kVec; ++e) {
+        const int c = threadIdx.x + e * 256;
+        if (c >= n4) continue;
+        const float f[4] = {v[e].x, v[e].y, v[e].z, v[e].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            q_lat[m * q_lora + 4 * c + k] = cvt<T>(f[k] * inv_rms * cvt<float>(gain[4 * c + k]));
+    }
+}
+
+template <typename T>
+mla_status_t launch_lat_norm(const acc_t<T>* P1, int splits, const T* gain, T* q_lat, int64_t M, int64_t q_lora,
+                             double eps, cudaStream_t st) {
+    if constexpr (std::is_same<acc_t<T>, float>::value) {
+        if (q_lora % 4 == 0 && q_lora <= 2048) {
+            lat_norm_vec_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, splits, gain, q_lat, M, q_lora, float(eps));
+            return check_launch("q latent RMSNorm (2a-norm)");
+        }
+    }
+    lat_norm_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, splits, gain, q_lat, M, q_lora, acc_t<T>(eps));
+    return check_launch("q latent RMSNorm (2a-norm)");
+}
+
+// Vectorised 2b for an fp32 accumulator: one warp per (token, head), float4 loads
+// of the split-K partials; same arithmetic as rope_gather_kernel.
+template <typename NopeT>
+__device__ __forceinline__ void store4(NopeT* dst, float a, float b, float c, float d) {
+    if constexpr (std::is_same<NopeT, float>::value) {
+        *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+    } else {
+        dst[0] = cvt<NopeT>(a); dst[1] = cvt<NopeT>(b); dst[2] = cvt<NopeT>(c); dst[3] = cvt<NopeT>(d);
+    }
+}
+
+template <typename T, typename NopeT>
+__global__ void __launch_bounds__(256) rope_gather_vec_kernel(
+    const float* __restrict__ P2, int splits, NopeT* __restrict__ q_nope, T* __restrict__ q_rope,
+    int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, const float* __restrict__ cs)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t qk = nope + rope;
+    const int64_t ncols = heads * qk;
+    const int64_t rows = M * heads;
+    for (int64_t mh = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; mh < rows;
+         mh += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+        const int64_t m = mh / heads, h = mh - m * heads;
+        const float* src = P2 + m * ncols + h * qk;
+        const int64_t zstride = M * ncols;
+        auto sum4 = [&](int64_t col) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int z = 0; z < splits; ++z) {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(src + z * zstride + col));
+                v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+            }
+            return v;
+        };
+        for (int64_t c = 4 * lane; c < nope; c += 128) {
+            const float4 v = sum4(c);
+            store4<NopeT>(q_nope + mh * nope + c, v.x, v.y, v.z, v.w);
+        }
+        const float* t = cs + 2 * ((m % sq) * (rope / 2));
+        for (int64_t c = 4 * lane; c < rope; c += 128) {
+            const float4 v = sum4(nope + c);                   // pairs j = c/2 and c/2 + 1
+            const int64_t j = c / 2;
+            const float c0 = t[2 * j], s0 = t[2 * j + 1], c1 = t[2 * j + 2], s1 = t[2 * j + 3];
+            T* o = q_rope + mh * rope + c;
+            o[0] = cvt<T>(v.x * c0 - v.y * s0);
+            o[1] = cvt<T>(v.x * s0 + v.y * c0);
+            o[2] = cvt<T>(v.z * c1 - v.w * s1);
+            o[3] = cvt<T>(v.z * s1 + v.w * c1);
+        }
+    }
+}
+
+template <typename T, typename NopeT>
+mla_status_t launch_rope_gather(const acc_t<T>* P2, int splits, const int64_t* positions, NopeT* q_nope, T* q_rope,
+                                int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope,
+                                const acc_t<T>* cs, cudaStream_t st) {
+    if constexpr (std::is_same<acc_t<T>, float>::value) {
+        if (nope % 4 == 0 && rope % 4 == 0) {
+            int64_t blocks = ceil_div(M * heads, 8);
+            if (blocks > 32LL * sm_count()) blocks = 32LL * sm_count();
+            rope_gather_vec_kernel<T, NopeT><<<unsigned(blocks), 256, 0, st>>>(P2, splits, q_nope, q_rope, M, sq,
+                                                                             heads, nope, rope, cs);
+            return check_launch("q rope (2b)");
+        }
+    }
+    const int64_t total = M * heads * (nope + rope / 2);
+    int64_t blocks = ceil_div(total, 256);
+    const int64_t cap = 16LL * sm_count();
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    rope_gather_kernel<T, NopeT><<<unsigned(blocks), 256, 0, st>>>(P2, splits, positions, q_nope, q_rope, M, sq,
+                                                                   heads, nope, rope, cs);
+    return check_launch("q rope (2b)");
+}
+
 // 2c: q_absorbed[m, h, :] = q_nope[m, h, :] @ W_uk[h]. grid = (n tiles, m tiles, heads).
 template <typename T, typename Acc>
 struct AbsorbProblem {
@@ -324,9 +456,7 @@ mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
     } else {
         MLA_TRY((launch_proj<CfgBig<Acc>, T, T>(x, Wqa, P1, M, a.q_lora, a.hidden, p.split1, p.chunk1, st)));
     }
-    lat_norm_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, p.split1, static_cast<const T*>(a.q_norm_w),
-                                                     q_lat, M, a.q_lora, Acc(a.eps));
-    MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
+    MLA_TRY(launch_lat_norm<T>(P1, p.split1, static_cast<const T*>(a.q_norm_w), q_lat, M, a.q_lora, a.eps, st));
     if (p.small) {
         MLA_TRY((launch_proj<CfgSmall<Acc>, T, T>(q_lat, Wqb, P2, M, ncols, a.q_lora, p.split2, p.chunk2, st)));
     } else {
@@ -341,19 +471,12 @@ mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
         tab.inv_freq[j] = Acc(1) / Acc(pw);
     }
     {
-        const int64_t total = M * a.heads * (a.nope + a.rope / 2);
-        int64_t blocks = ceil_div(total, 256);
-        const int64_t cap = 16LL * sm_count();
-        if (blocks > cap) blocks = cap;
-        if (blocks < 1) blocks = 1;
         Acc* cs = reinterpret_cast<Acc*>(ws + p.off_cs);
-        rope_table_kernel<T><<<unsigned(ceil_div(a.sq * (a.rope / 2), 256) > 0 ? ceil_div(a.sq * (a.rope / 2), 256) : 1), 256, 0, st>>>(a.positions, a.sq,
-                                                                                               a.rope / 2, tab, cs);
+        const int64_t tblocks = ceil_div(a.sq * (a.rope / 2), 256);
+        rope_table_kernel<T><<<unsigned(tblocks > 0 ? tblocks : 1), 256, 0, st>>>(a.positions, a.sq, a.rope / 2, tab, cs);
         MLA_TRY(check_launch("q rope table"));
-        rope_gather_kernel<T><<<unsigned(blocks), 256, 0, st>>>(
-            P2, p.split2, a.positions, q_nope, static_cast<T*>(a.q_rope),
-            M, a.sq, a.heads, a.nope, a.rope, cs);
-        MLA_TRY(check_launch("q rope (2b)"));
+        MLA_TRY((launch_rope_gather<T, Acc>(P2, p.split2, a.positions, q_nope, static_cast<T*>(a.q_rope), M, a.sq,
+                                            a.heads, a.nope, a.rope, cs, st)));
     }
     if (p.small) {
         MLA_TRY((launch_absorb<CfgSmall<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk),
@@ -461,9 +584,7 @@ mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3) {
     g1.C = P1; g1.c_is_t = false; g1.c_ldm = a.q_lora; g1.c_ldz = M * a.q_lora; g1.bn = 128; g1.err = err; g1.split3 = split3;
     MLA_TRY(tc_gemm<T>(g1, st));
 
-    lat_norm_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, p.split1, static_cast<const T*>(a.q_norm_w), q_lat, M,
-                                                     a.q_lora, Acc(a.eps));
-    MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
+    MLA_TRY(launch_lat_norm<T>(P1, p.split1, static_cast<const T*>(a.q_norm_w), q_lat, M, a.q_lora, a.eps, st));
 
     TcGemm g2{};   // 2a2: q_lat [M, q_lora] @ W_q_b [q_lora, H*(nope+rope)]
     g2.A = q_lat; g2.a_dims[0] = a.q_lora; g2.a_dims[1] = 1; g2.a_dims[2] = M; g2.a_ld[0] = a.q_lora; g2.a_ld[1] = a.q_lora;
@@ -479,21 +600,14 @@ mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3) {
         tab.inv_freq[j] = Acc(1) / Acc(pw);
     }
     {
-        const int64_t total = M * a.heads * (a.nope + a.rope / 2);
-        int64_t blocks = ceil_div(total, 256);
-        const int64_t cap = 16LL * sm_count();
-        if (blocks > cap) blocks = cap;
-        if (blocks < 1) blocks = 1;
         // q_nope in the storage dtype: the left operand of the 2c tensor-core GEMM,
         // whose operands share one dtype
         Acc* cs = reinterpret_cast<Acc*>(ws + p.off_cs);
-        rope_table_kernel<T><<<unsigned(ceil_div(a.sq * (a.rope / 2), 256) > 0 ? ceil_div(a.sq * (a.rope / 2), 256) : 1), 256, 0, st>>>(a.positions, a.sq,
-                                                                                               a.rope / 2, tab, cs);
+        const int64_t tblocks = ceil_div(a.sq * (a.rope / 2), 256);
+        rope_table_kernel<T><<<unsigned(tblocks > 0 ? tblocks : 1), 256, 0, st>>>(a.positions, a.sq, a.rope / 2, tab, cs);
         MLA_TRY(check_launch("q rope table"));
-        rope_gather_kernel<T, T><<<unsigned(blocks), 256, 0, st>>>(P2, p.split2, a.positions, q_nope_t,
-                                                                    static_cast<T*>(a.q_rope), M, a.sq, a.heads,
-                                                                    a.nope, a.rope, cs);
-        MLA_TRY(check_launch("q rope (2b)"));
+        MLA_TRY((launch_rope_gather<T, T>(P2, p.split2, a.positions, q_nope_t, static_cast<T*>(a.q_rope), M, a.sq,
+                                          a.heads, a.nope, a.rope, cs, st)));
     }
     TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h]
     g3.A = q_nope_t; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;

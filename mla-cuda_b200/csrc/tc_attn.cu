@@ -581,62 +581,75 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             constexpr int kP = kStgRows * (kRope / 4) / kConvThreads;   // pe float4 pieces per thread (CTA 1)
             static_assert(kU * kConvThreads == kStgRows * (kHalf / 4) && kP * kConvThreads == kStgRows * (kRope / 4),
                           "converter mapping");
-            bool okc = true;
-            for (int64_t i = 0; okc && i < n; ++i) {
-                const int sl = int(i % Tr::kSlots);
-                if (!MLA_TW(10, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                                          ERR_TIMEOUT_BASE + 11)))
-                    break;
-                if (ct == 0) trace_put(p, 3, i * 16 + 2);
-                unsigned char* buf = slots + sl * kSlotBytes;
-                for (int h = 0; h < 2; ++h) {
-                    const int64_t k = 2 * i + h;
-                    const int st = int(k % Tr::kStages);
-                    if (!MLA_TW(9, mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
-                                             ERR_TIMEOUT_BASE + 10))) {
-                        okc = false;
+            // specialised per rank at compile time: CTA 1 also converts the rope dims
+            auto convert = [&](auto rope_tag) {
+                constexpr bool kR = decltype(rope_tag)::value;
+                bool okc = true;
+                for (int64_t i = 0; okc && i < n; ++i) {
+                    const int sl = int(i % Tr::kSlots);
+                    if (!MLA_TW(10, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                                              ERR_TIMEOUT_BASE + 11)))
                         break;
-                    }
-                    const float4* src = reinterpret_cast<const float4*>(stg + st * kStgBytes);
-                    uint2 cv[kU], pv[kP];
-#pragma unroll
-                    for (int q = 0; q < kU; ++q) {
-                        const float4 a = src[ct + q * kConvThreads];
-                        cv[q] = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
-                    }
-                    if (rank == 1) {
-                        const float4* pe = src + kStgRows * (kHalf / 4);
-#pragma unroll
-                        for (int q = 0; q < kP; ++q) {
-                            const float4 a = pe[ct + q * kConvThreads];
-                            pv[q] = make_uint2(pack_bf16(a.x, a.y), pack_bf16(a.z, a.w));
+                    if (ct == 0) trace_put(p, 3, i * 16 + 2);
+                    unsigned char* buf = slots + sl * kSlotBytes;
+                    for (int h = 0; h < 2; ++h) {
+                        const int64_t k = 2 * i + h;
+                        const int st = int(k % Tr::kStages);
+                        if (!MLA_TW(9, mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
+                                                 ERR_TIMEOUT_BASE + 10))) {
+                            okc = false;
+                            break;
                         }
+                        MLA_PROF(long long tc0 = clock64();)
+                        const float4* src = reinterpret_cast<const float4*>(stg + st * kStgBytes);
+                        uint2 cv[kU], pv[kP];
+                        float4 a[kU], b[kP];
+                        // all loads of the half tile first, then the conversions
+    #pragma unroll
+                        for (int q = 0; q < kU; ++q) a[q] = src[ct + q * kConvThreads];
+                        if constexpr (kR) {
+    #pragma unroll
+                            for (int q = 0; q < kP; ++q) b[q] = src[kStgRows * (kHalf / 4) + ct + q * kConvThreads];
+                        }
+    #pragma unroll
+                        for (int q = 0; q < kU; ++q) cv[q] = make_uint2(pack_bf16(a[q].x, a[q].y), pack_bf16(a[q].z, a[q].w));
+                        if constexpr (kR) {
+    #pragma unroll
+                            for (int q = 0; q < kP; ++q) pv[q] = make_uint2(pack_bf16(b[q].x, b[q].y), pack_bf16(b[q].z, b[q].w));
+                        }
+                        MLA_PROF(wacc[16] += clock64() - tc0; tc0 = clock64();)
+                        // my generic-proxy reads of the staging buffer must be ordered before
+                        // the next TMA (async-proxy) write into it
+                        fence_proxy_async_smem();
+                        mbar_arrive(&bars->stg_empty[st]);
+                        MLA_PROF(wacc[17] += clock64() - tc0; tc0 = clock64();)
+    #pragma unroll
+                        for (int q = 0; q < kU; ++q) {
+                            const int f = ct + q * kConvThreads;          // float4 index in the half tile
+                            const int r = h * kStgRows + (f >> 6), c4 = f & 63;
+                            const int chunk = c4 >> 4, unit = ((c4 & 15) >> 1) ^ (r & 7);
+                            *reinterpret_cast<uint2*>(buf + chunk * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = cv[q];
+                        }
+                        if constexpr (kR) {
+    #pragma unroll
+                            for (int q = 0; q < kP; ++q) {
+                                const int f = ct + q * kConvThreads;
+                                const int r = h * kStgRows + (f >> 4), c4 = f & 15;
+                                const int unit = (c4 >> 1) ^ (r & 7);
+                                *reinterpret_cast<uint2*>(buf + 4 * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = pv[q];
+                            }
+                        }
+                        MLA_PROF(wacc[18] += clock64() - tc0;)
                     }
-                    // my generic-proxy reads of the staging buffer must be ordered before
-                    // the next TMA (async-proxy) write into it
+                    if (!okc) break;
+                    MLA_PROF(const long long tf0 = clock64();)
                     fence_proxy_async_smem();
-                    mbar_arrive(&bars->stg_empty[st]);
-#pragma unroll
-                    for (int q = 0; q < kU; ++q) {
-                        const int f = ct + q * kConvThreads;          // float4 index in the half tile
-                        const int r = h * kStgRows + (f >> 6), c4 = f & 63;
-                        const int chunk = c4 >> 4, unit = ((c4 & 15) >> 1) ^ (r & 7);
-                        *reinterpret_cast<uint2*>(buf + chunk * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = cv[q];
-                    }
-                    if (rank == 1) {
-#pragma unroll
-                        for (int q = 0; q < kP; ++q) {
-                            const int f = ct + q * kConvThreads;
-                            const int r = h * kStgRows + (f >> 4), c4 = f & 15;
-                            const int unit = (c4 >> 1) ^ (r & 7);
-                            *reinterpret_cast<uint2*>(buf + 4 * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = pv[q];
-                        }
-                    }
+                    mbar_arrive(&bars->bf_full[sl]);
+                    MLA_PROF(wacc[19] += clock64() - tf0;)
                 }
-                if (!okc) break;
-                fence_proxy_async_smem();
-                mbar_arrive(&bars->bf_full[sl]);
-            }
+            };
+            if (rank == 1) convert(std::true_type{});
+            else convert(std::false_type{});
           }
         }
     }
@@ -657,6 +670,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             trace_put(p, 24, wacc[16] / 1000);
             trace_put(p, 25, wacc[17] / 1000);
         }
+        if (warp == 2 && lane == 0)
+            for (int k = 0; k < 4; ++k) trace_put(p, 28 + k, wacc[16 + k] / 1000);
     }
 #endif
     if (threadIdx.x == 0) trace_put(p, 4, 1);
@@ -878,9 +893,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                 const volatile int* t = trace_host + b * 32;
                 fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d | kcyc total %d "
                         "stg_empty %d bf_empty(p) %d p_full %d q_ready %d bf_full %d s_full %d x_full %d o_resc %d "
-                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d pv_issue %d s_issue %d | cmp_pre %d p_store %d\n",
+                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d pv_issue %d s_issue %d | cmp_pre %d p_store %d | conv ld %d fence1 %d st %d fence2 %d\n",
                         (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[23], t[8], t[9], t[10], t[11], t[12],
-                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25], t[26], t[27]);
+                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25], t[26], t[27], t[28], t[29], t[30], t[31]);
             }
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);

@@ -310,6 +310,221 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ------------------------------------------------------------ persistent form
+// One CTA per SM walks the output tiles (units) u = blockIdx.x, +gridDim.x, ...
+// (N tile fastest, then M tile, then launch index z). The shared-memory ring runs
+// on across units, and the accumulator is double-buffered in TMEM (2 x BN
+// columns), so the epilogue of one unit overlaps the loads and MMAs of the next.
+template <int BN> constexpr int pstages() { return BN == 256 ? 4 : 6; }
+template <int BN> constexpr size_t psmem_bytes() {
+    return 1024 + size_t(pstages<BN>()) * (a_bytes() + b_bytes<BN>()) + 256;
+}
+
+struct Units {
+    int64_t nt, mt, total;   // N tiles, M tiles, all units
+};
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
+    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Run r, const Units U)
+{
+    constexpr int S = pstages<BN>();
+    constexpr int BK = tc_gemm_bk<T>();
+    constexpr int kInstK = 32 / int(sizeof(T));
+    constexpr int kStage = a_bytes() + b_bytes<BN>();
+    constexpr uint32_t kTmemCols = 2u * BN;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStage);
+    uint64_t* empty = full + S;
+    uint64_t* acc_full = empty + S;     // [2]
+    uint64_t* acc_empty = acc_full + 2; // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+    volatile int* abort = abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // unit u -> (z, m0, n0) and its K range
+    auto unit = [&](int64_t u, int& z, int64_t& m0, int64_t& n0, int64_t& kb, int64_t& nkb) {
+        const int64_t per_z = U.nt * U.mt;
+        z = int(u / per_z);
+        const int64_t rem = u - int64_t(z) * per_z;
+        m0 = (rem / U.nt) * 128;
+        n0 = (rem % U.nt) * BN;
+        kb = int64_t(z % r.spb) * r.k_chunk;
+        const int64_t ke = min(r.K, kb + r.k_chunk);
+        nkb = ke > kb ? (ke - kb + BK - 1) / BK : 0;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        int64_t it = 0;                      // k blocks issued so far (ring position)
+        bool ok = true;
+        for (int64_t u = blockIdx.x; u < U.total && ok; u += gridDim.x) {
+            int z; int64_t m0, n0, kb, nkb;
+            unit(u, z, m0, n0, kb, nkb);
+            const int ya = z / r.spb;
+            for (int64_t i = 0; i < nkb; ++i, ++it) {
+                const int s = int(it % S);
+                if (!mbar_wait(&empty[s], uint32_t(((it / S) & 1) ^ 1), abort, r.err, ERR_TIMEOUT_BASE + 11)) {
+                    ok = false;
+                    break;
+                }
+                const int32_t k = int32_t(kb + i * BK);
+                unsigned char* st = smem + s * kStage;
+                mbar_arrive_expect_tx(&full[s], uint32_t(kStage));
+                if (r.a_batch_outer) tma_load_3d(st, &tmA, &full[s], k, int32_t(m0), ya);
+                else tma_load_3d(st, &tmA, &full[s], k, ya, int32_t(m0));
+                unsigned char* bdst = st + a_bytes();
+                if (r.b_mn) {
+                    for (int g = 0; g < BN / BK; ++g)
+                        tma_load_3d(bdst + g * (BK * 128), &tmB, &full[s], int32_t(n0 + g * BK), k, ya);
+                } else {
+                    tma_load_3d(bdst, &tmB, &full[s], k, int32_t(n0), ya);
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        const uint32_t idesc = instr_desc(fmt<T>(), 128, BN, 0, r.b_mn ? 1u : 0u);
+        constexpr bool kA32 = sizeof(T) == 4;
+        int64_t it = 0, lt = 0;
+        bool ok = true;
+        for (int64_t u = blockIdx.x; u < U.total && ok; u += gridDim.x, ++lt) {
+            int z; int64_t m0, n0, kb, nkb;
+            unit(u, z, m0, n0, kb, nkb);
+            const int buf = int(lt & 1);
+            if (!mbar_wait(&acc_empty[buf], uint32_t(((lt >> 1) & 1) ^ 1), abort, r.err, ERR_TIMEOUT_BASE + 12)) break;
+            tc_fence_after();
+            const uint32_t d = tmem + uint32_t(buf) * BN;
+            for (int64_t i = 0; i < nkb; ++i, ++it) {
+                const int s = int(it % S);
+                if (!mbar_wait(&full[s], uint32_t((it / S) & 1), abort, r.err, ERR_TIMEOUT_BASE + 13)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(smem + s * kStage);
+                const uint32_t b0 = a0 + a_bytes();
+                const uint64_t ad0 = smem_desc(a0, 16, 1024, 2);
+                const uint64_t bd0 = r.b_mn ? smem_desc(b0, BK * 128, kA32 ? 512 : 1024, kA32 ? 1 : 2)
+                                            : smem_desc(b0, 16, 1024, 2);
+#pragma unroll
+                for (int kk = 0; kk < BK / kInstK; ++kk) {
+                    const uint64_t ad = ad0 + uint64_t((kk * 32) >> 4);
+                    const uint64_t bd = bd0 + uint64_t((r.b_mn ? kk * (kInstK * 128) : kk * 32) >> 4);
+                    const uint32_t acc = (i | kk) ? 1u : 0u;
+                    if constexpr (std::is_same<T, float>::value) mma_ss_tf32(d, ad, bd, idesc, acc);
+                    else mma_ss(d, ad, bd, idesc, acc);
+                }
+                mma_commit(&empty[s]);
+            }
+            if (!ok) break;
+            mma_commit(&acc_full[buf]);
+        }
+    } else if (warp >= 2) {
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_off = uint32_t(q * 32) << 16;
+        int64_t lt = 0;
+        for (int64_t u = blockIdx.x; u < U.total; u += gridDim.x, ++lt) {
+            int z; int64_t m0, n0, kb, nkb;
+            unit(u, z, m0, n0, kb, nkb);
+            const int buf = int(lt & 1);
+            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], uint32_t((lt >> 1) & 1), abort, r.err,
+                                                   ERR_TIMEOUT_BASE + 14)))
+                break;
+            tc_fence_after();
+            const int64_t m = m0 + row;
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                if (nkb > 0) {
+                    tmem_ld32(tmem + lane_off + uint32_t(buf) * BN + c * 32, v);
+                    tmem_ld_wait();
+                } else {
+                    for (int e = 0; e < 32; ++e) v[e] = 0u;
+                }
+                const int64_t n = n0 + c * 32;
+                if (m >= r.M || n >= r.N) continue;
+                const int64_t off = m * r.c_ldm + int64_t(z) * r.c_ldz + n;
+                if (!r.c_is_t || std::is_same<T, float>::value) {
+                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(r.C) + off);
+                    for (int e = 0; e < 8; ++e)
+                        dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                                             __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
+                } else {
+                    uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(r.C) + off);
+                    for (int e = 0; e < 4; ++e) {
+                        uint32_t w[4];
+                        for (int h = 0; h < 4; ++h) {
+                            const float lo_ = __uint_as_float(v[8 * e + 2 * h]), hi = __uint_as_float(v[8 * e + 2 * h + 1]);
+                            if constexpr (std::is_same<T, __half>::value) {
+                                __half2 h2 = __floats2half2_rn(lo_, hi);
+                                w[h] = *reinterpret_cast<uint32_t*>(&h2);
+                            } else {
+                                w[h] = pack_bf16(lo_, hi);
+                            }
+                        }
+                        dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) { }
+    }
+    tc_fence_after();
+    __syncwarp();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <typename T, int BN>
+mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
+    constexpr int BK = tc_gemm_bk<T>();
+    CUtensorMap ta, tb;
+    const uint32_t abox[3] = {uint32_t(BK), g.a_batch_outer ? 128u : 1u, g.a_batch_outer ? 1u : 128u};
+    const uint32_t bbox_mn[3] = {uint32_t(BK), uint32_t(BK), 1u};
+    const uint32_t bbox_k[3] = {uint32_t(BK), uint32_t(BN), 1u};
+    if (!make_map_3d<T>(&ta, g.A, g.a_dims, g.a_ld, abox, true) ||
+        !make_map_3d<T>(&tb, g.B, g.b_dims, g.b_ld, g.b_mn ? bbox_mn : bbox_k, true,
+                        /*atom32=*/g.b_mn && sizeof(T) == 4))
+        return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
+    Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
+          g.c_is_t ? 1 : 0, 0, g.a_batch_outer ? 1 : 0, g.C, g.c_ldm, g.c_ldz, g.err};
+    Units U{ceil_div(g.N, BN), ceil_div(g.M, 128), 0};
+    U.total = U.nt * U.mt * g.Z;
+    auto kern = tc_gemm_persist_kernel<T, BN>;
+    const size_t smem = psmem_bytes<BN>();
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    const int64_t grid = U.total < sm_count() ? U.total : sm_count();
+    kern<<<unsigned(grid), kThreads, smem, st>>>(ta, tb, r, U);
+    return check_launch("tensor-core GEMM (persistent)");
+}
+
 template <typename T, int BN, bool S3>
 mla_status_t launch(const TcGemm& g, cudaStream_t st) {
     constexpr int BK = tc_gemm_bk<T>();
@@ -333,6 +548,12 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
 
 }  // namespace tcg
 
+// MLA_GEMM_CLASSIC=1 (debug): one CTA per output tile instead of the persistent form.
+static bool tc_gemm_classic() {
+    static const bool v = getenv("MLA_GEMM_CLASSIC") != nullptr && getenv("MLA_GEMM_CLASSIC")[0] == '1';
+    return v;
+}
+
 template <typename T>
 mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
     if constexpr (std::is_same<T, double>::value) {
@@ -345,6 +566,10 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
             if (g.split3) return tcg::launch<T, 128, true>(g, st);
         } else {
             if (g.split3) return set_error(MLA_ERR_UNSUPPORTED, "MLA: 3xTF32 needs fp32 operands");
+        }
+        if (!g.c_accum && !tc_gemm_classic()) {
+            if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
+            return tcg::launch_persist<T, 128>(g, st);
         }
         if (g.bn == 256) return tcg::launch<T, 256, false>(g, st);
         return tcg::launch<T, 128, false>(g, st);
