@@ -468,21 +468,21 @@ mla_status_t attn_exact_t3(const AArgs& a, cudaStream_t st) {
     if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
         return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
 
-    // S[b] = q_absorbed[b] [rows_b, R] @ c_kv[b]^T; keys past sk read as zeros (TMA
-    // fill) and land in the padding columns [sk, ld)
+    // S[b] = q_absorbed[b] [rows_b, R] @ c_kv[b]^T + q_rope[b] @ pe[b]^T in one GEMM (the
+    // rope pair is a second K phase); keys past sk read as zeros (TMA fill) and land
+    // in the padding columns [sk, ld)
     TcGemm g1{};
     g1.A = a.q_absorbed; g1.a_dims[0] = a.kv_rank; g1.a_dims[1] = a.batch; g1.a_dims[2] = p.rows_b;
     g1.a_ld[0] = p.rows_b * a.kv_rank; g1.a_ld[1] = a.kv_rank;
     g1.B = a.c_kv; g1.b_mn = false; g1.b_dims[0] = a.kv_rank; g1.b_dims[1] = a.sk; g1.b_dims[2] = a.batch;
     g1.b_ld[0] = a.kv_rank; g1.b_ld[1] = a.sk * a.kv_rank;
+    g1.A2 = a.q_rope; g1.a2_dims[0] = a.rope; g1.a2_dims[1] = a.batch; g1.a2_dims[2] = p.rows_b;
+    g1.a2_ld[0] = p.rows_b * a.rope; g1.a2_ld[1] = a.rope;
+    g1.B2 = a.pe_cache; g1.b2_dims[0] = a.rope; g1.b2_dims[1] = a.sk; g1.b2_dims[2] = a.batch;
+    g1.b2_ld[0] = a.rope; g1.b2_ld[1] = a.sk * a.rope; g1.K2 = a.rope;
     g1.M = p.rows_b; g1.N = p.ld; g1.K = a.kv_rank; g1.Z = int(a.batch); g1.spb = 1; g1.k_chunk = a.kv_rank;
     g1.C = S; g1.c_ldm = p.ld; g1.c_ldz = p.rows_b * p.ld; g1.bn = 128; g1.split3 = true; g1.err = err;
     MLA_TRY(tc_gemm<float>(g1, st));
-    TcGemm g2 = g1;   // S[b] += q_rope[b] @ pe[b]^T
-    g2.A = a.q_rope; g2.a_dims[0] = a.rope; g2.a_ld[0] = p.rows_b * a.rope; g2.a_ld[1] = a.rope;
-    g2.B = a.pe_cache; g2.b_dims[0] = a.rope; g2.b_ld[0] = a.rope; g2.b_ld[1] = a.sk * a.rope;
-    g2.K = a.rope; g2.k_chunk = a.rope; g2.c_accum = true;
-    MLA_TRY(tc_gemm<float>(g2, st));
 
     {
         int64_t blocks = ceil_div(p.rows_total, 8);

@@ -32,6 +32,7 @@ enum : int { ERR_TIMEOUT_BASE = 200 };
 struct Run {
     int64_t M, N, K, k_chunk;
     int Z, spb, b_mn, c_is_t, c_accum, a_batch_outer;
+    int64_t nkb2;    // K blocks of the second operand pair (classic kernel only)
     void* C; int64_t c_ldm, c_ldz;
     int* err;
 };
@@ -59,7 +60,8 @@ template <int BN, bool S3> constexpr size_t smem_bytes() {
 
 template <typename T, int BN, bool S3>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
-    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Run r)
+    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, const Run r)
 {
     constexpr int S = stages<BN, S3>();
     constexpr int BK = tc_gemm_bk<T>();             // elements per 128-byte row
@@ -90,7 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     const int ya = z / r.spb;                       // batch
     const int64_t kb = int64_t(z % r.spb) * r.k_chunk;
     const int64_t ke = min(r.K, kb + r.k_chunk);
-    const int64_t nkb = ke > kb ? (ke - kb + BK - 1) / BK : 0;
+    const int64_t nkb1 = ke > kb ? (ke - kb + BK - 1) / BK : 0;
+    const int64_t nkb = nkb1 + r.nkb2;              // second operand pair (A2, B2) after the first
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -114,20 +117,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (r.nkb2 > 0) {
+            tma_prefetch_desc(&tmA2);
+            tma_prefetch_desc(&tmB2);
+        }
         for (int64_t i = 0; i < nkb; ++i) {
             const int s = int(i % S);
             if (!mbar_wait(&empty[s], uint32_t(((i / S) & 1) ^ 1), abort, r.err, ERR_TIMEOUT_BASE + 1)) break;
-            const int32_t k = int32_t(kb + i * BK);
+            const bool second = i >= nkb1;
+            const CUtensorMap* ma = second ? &tmA2 : &tmA;
+            const CUtensorMap* mb = second ? &tmB2 : &tmB;
+            const int32_t k = second ? int32_t((i - nkb1) * BK) : int32_t(kb + i * BK);
             unsigned char* st = smem + s * kStage;
             mbar_arrive_expect_tx(&full[s], uint32_t(kStage));
-            if (r.a_batch_outer) tma_load_3d(st, &tmA, &full[s], k, int32_t(m0), ya);
-            else tma_load_3d(st, &tmA, &full[s], k, ya, int32_t(m0));
+            if (r.a_batch_outer) tma_load_3d(st, ma, &full[s], k, int32_t(m0), ya);
+            else tma_load_3d(st, ma, &full[s], k, ya, int32_t(m0));
             unsigned char* bdst = st + a_bytes();
             if (r.b_mn) {
                 for (int g = 0; g < BN / BK; ++g)   // BK-wide column groups of N, BK rows of K each
-                    tma_load_3d(bdst + g * (BK * 128), &tmB, &full[s], int32_t(n0 + g * BK), k, ya);
+                    tma_load_3d(bdst + g * (BK * 128), mb, &full[s], int32_t(n0 + g * BK), k, ya);
             } else {
-                tma_load_3d(bdst, &tmB, &full[s], k, int32_t(n0), ya);
+                tma_load_3d(bdst, mb, &full[s], k, int32_t(n0), ya);
             }
         }
     } else if (warp == 1 && lane == 0) {
@@ -514,7 +524,7 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
                         /*atom32=*/g.b_mn && sizeof(T) == 4))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
-          g.c_is_t ? 1 : 0, 0, g.a_batch_outer ? 1 : 0, g.C, g.c_ldm, g.c_ldz, g.err};
+          g.c_is_t ? 1 : 0, 0, g.a_batch_outer ? 1 : 0, 0, g.C, g.c_ldm, g.c_ldz, g.err};
     Units U{ceil_div(g.N, BN), ceil_div(g.M, 128), 0};
     U.total = U.nt * U.mt * g.Z;
     auto kern = tc_gemm_persist_kernel<T, BN>;
@@ -536,13 +546,20 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
         !make_map_3d<T>(&tb, g.B, g.b_dims, g.b_ld, g.b_mn ? bbox_mn : bbox_k, true,
                         /*atom32=*/g.b_mn && sizeof(T) == 4))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
+    CUtensorMap ta2 = ta, tb2 = tb;
+    if (g.K2 > 0 &&
+        (!make_map_3d<T>(&ta2, g.A2, g.a2_dims, g.a2_ld, abox, true) ||
+         !make_map_3d<T>(&tb2, g.B2, g.b2_dims, g.b2_ld, g.b_mn ? bbox_mn : bbox_k, true,
+                         /*atom32=*/g.b_mn && sizeof(T) == 4)))
+        return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
-          g.c_is_t ? 1 : 0, g.c_accum ? 1 : 0, g.a_batch_outer ? 1 : 0, g.C, g.c_ldm, g.c_ldz, g.err};
+          g.c_is_t ? 1 : 0, g.c_accum ? 1 : 0, g.a_batch_outer ? 1 : 0, g.K2 > 0 ? ceil_div(g.K2, BK) : 0,
+          g.C, g.c_ldm, g.c_ldz, g.err};
     auto kern = tc_gemm_kernel<T, BN, S3>;
     const size_t smem = smem_bytes<BN, S3>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     dim3 grid(unsigned(ceil_div(g.N, BN)), unsigned(ceil_div(g.M, 128)), unsigned(g.Z));
-    kern<<<grid, kThreads, smem, st>>>(ta, tb, r);
+    kern<<<grid, kThreads, smem, st>>>(ta, tb, ta2, tb2, r);
     return check_launch("tensor-core GEMM");
 }
 
@@ -567,7 +584,7 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
         } else {
             if (g.split3) return set_error(MLA_ERR_UNSUPPORTED, "MLA: 3xTF32 needs fp32 operands");
         }
-        if (!g.c_accum && !tc_gemm_classic()) {
+        if (!g.c_accum && g.K2 == 0 && !tc_gemm_classic()) {
             if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
             return tcg::launch_persist<T, 128>(g, st);
         }

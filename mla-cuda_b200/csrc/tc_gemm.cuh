@@ -30,6 +30,11 @@ struct TcGemm {
     void* C; bool c_is_t; bool c_accum; int64_t c_ldm, c_ldz;
     int bn;          // 128 or 256 output columns per CTA
     bool split3;
+    // optional second operand pair, accumulated after A*B: C += A2*B2 over K2
+    // (same layouts and boxes as A / B; spb must be 1)
+    const void* A2; int64_t a2_dims[3]; int64_t a2_ld[2];
+    const void* B2; int64_t b2_dims[3]; int64_t b2_ld[2];
+    int64_t K2;
     int* err;        // device error word (bounded waits)
 };
 
