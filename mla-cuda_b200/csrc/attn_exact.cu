@@ -394,6 +394,38 @@ __global__ void __launch_bounds__(256) softmax_rows_kernel(
     }
 }
 
+// Non-causal rows: the row max comes from the per-tile maxima the score GEMM
+// wrote, so the scores are read once. One warp per row, 16-byte accesses.
+__global__ void __launch_bounds__(256) softmax_rows_tilemax_kernel(
+    float* __restrict__ S, const float* __restrict__ tile_max, int ntiles, float* __restrict__ row_max,
+    float* __restrict__ row_sum, int64_t rows_total, int64_t ld, int64_t sk, float scale)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t g = blockIdx.x * 8LL + warp; g < rows_total; g += int64_t(gridDim.x) * 8) {
+        float mx = neg_inf<float>();
+        for (int t = lane; t < ntiles; t += 32) mx = fmaxf(mx, tile_max[g * ntiles + t]);
+        for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        mx = mx / scale;                      // max(S) / scale == max(S / scale) for scale > 0
+        float4* srow = reinterpret_cast<float4*>(S + g * ld);
+        float l = 0.f;
+        for (int64_t c = lane; 4 * c < sk; c += 32) {
+            float4 v = srow[c];
+            const int64_t k = 4 * c;
+            v.x = fexp(v.x / scale - mx);
+            v.y = k + 1 < sk ? fexp(v.y / scale - mx) : 0.f;
+            v.z = k + 2 < sk ? fexp(v.z / scale - mx) : 0.f;
+            v.w = k + 3 < sk ? fexp(v.w / scale - mx) : 0.f;
+            srow[c] = v;
+            l += (v.x + v.y) + (v.z + v.w);
+        }
+        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        if (lane == 0) {
+            row_max[g] = mx;
+            row_sum[g] = l;
+        }
+    }
+}
+
 // ctx[g, :] = sum over key slices of the partial products / l[g]; lse[g] = M + log l.
 // parts: [batch][slices][rows_b][R]; ctx: [rows_total][R] with g = b * rows_b + row.
 __global__ void __launch_bounds__(256) ctx_reduce_kernel(
@@ -419,9 +451,9 @@ __global__ void __launch_bounds__(256) ctx_reduce_kernel(
 }
 
 struct T3Plan {
-    int64_t rows_b, rows_total, ld, chunk;
+    int64_t rows_b, rows_total, ld, chunk, ntiles;
     int slices;
-    size_t off_err, off_S, off_max, off_sum, off_parts, off_ctx, total;
+    size_t off_err, off_S, off_tmax, off_max, off_sum, off_parts, off_ctx, total;
 };
 
 T3Plan make_t3plan(const AArgs& a) {
@@ -429,19 +461,27 @@ T3Plan make_t3plan(const AArgs& a) {
     p.rows_b = a.sq * a.heads;
     p.rows_total = a.batch * p.rows_b;
     p.ld = (a.sk + 31) / 32 * 32;
-    // key slices of P @ c_kv: fill about two waves of SMs, at least 8 K blocks each
+    // key slices of P @ c_kv (one CTA per SM): the slice count in 1..8 whose CTAs fill
+    // their last wave best, at least 8 K blocks per slice
     const int64_t tiles = ceil_div(p.rows_b, 128) * ceil_div(a.kv_rank, 128) * a.batch;
     const int64_t kblocks = ceil_div(a.sk, 32);
-    int64_t s = (2LL * sm_count()) / (tiles > 0 ? tiles : 1);
-    if (s > kblocks / 8) s = kblocks / 8;
-    if (s > 65535 / (a.batch > 0 ? a.batch : 1)) s = 65535 / (a.batch > 0 ? a.batch : 1);
-    if (s < 1) s = 1;
+    const int64_t sms = sm_count();
+    int64_t s = 1;
+    double best = 0.0;
+    for (int64_t c = 1; c <= 8 && c <= kblocks / 8; ++c) {
+        if (c * a.batch > 65535) break;
+        const int64_t ctas = tiles * c;
+        const double fill = double(ctas) / double(ceil_div(ctas, sms) * sms);
+        if (fill > best + 0.02) { best = fill; s = c; }
+    }
     const int64_t cb = ceil_div(kblocks, s);
     p.chunk = cb * 32;
     p.slices = int(ceil_div(kblocks, cb));
     size_t off = 0;
     p.off_err = off;   off = align_up(off + 256, 256);
     p.off_S = off;     off = align_up(off + size_t(p.rows_total) * p.ld * sizeof(float), 256);
+    p.ntiles = ceil_div(p.ld, 128);
+    p.off_tmax = off;  off = align_up(off + size_t(p.rows_total) * p.ntiles * sizeof(float), 256);
     p.off_max = off;   off = align_up(off + size_t(p.rows_total) * sizeof(float), 256);
     p.off_sum = off;   off = align_up(off + size_t(p.rows_total) * sizeof(float), 256);
     p.off_parts = off; off = align_up(off + size_t(p.slices) * p.rows_total * a.kv_rank * sizeof(float), 256);
@@ -482,13 +522,22 @@ mla_status_t attn_exact_t3(const AArgs& a, cudaStream_t st) {
     g1.b2_ld[0] = a.rope; g1.b2_ld[1] = a.sk * a.rope; g1.K2 = a.rope;
     g1.M = p.rows_b; g1.N = p.ld; g1.K = a.kv_rank; g1.Z = int(a.batch); g1.spb = 1; g1.k_chunk = a.kv_rank;
     g1.C = S; g1.c_ldm = p.ld; g1.c_ldz = p.rows_b * p.ld; g1.bn = 128; g1.split3 = true; g1.err = err;
+    float* tmax = reinterpret_cast<float*>(ws + p.off_tmax);
+    if (!a.causal) {   // per-tile row maxima for the one-pass softmax
+        g1.rowmax = tmax;
+        g1.n_valid = a.sk;
+    }
     MLA_TRY(tc_gemm<float>(g1, st));
 
     {
         int64_t blocks = ceil_div(p.rows_total, 8);
         if (blocks > 16LL * sm_count()) blocks = 16LL * sm_count();
-        softmax_rows_kernel<<<unsigned(blocks), 256, 0, st>>>(S, rmax, rsum, p.rows_total, p.ld, a.sk, a.sq,
-                                                              a.heads, float(a.scale), a.causal);
+        if (!a.causal)
+            softmax_rows_tilemax_kernel<<<unsigned(blocks), 256, 0, st>>>(S, tmax, int(p.ntiles), rmax, rsum,
+                                                                          p.rows_total, p.ld, a.sk, float(a.scale));
+        else
+            softmax_rows_kernel<<<unsigned(blocks), 256, 0, st>>>(S, rmax, rsum, p.rows_total, p.ld, a.sk, a.sq,
+                                                                  a.heads, float(a.scale), a.causal);
         MLA_TRY(check_launch("attention softmax rows"));
     }
 

@@ -33,6 +33,7 @@ struct Run {
     int64_t M, N, K, k_chunk;
     int Z, spb, b_mn, c_is_t, c_accum, a_batch_outer;
     int64_t nkb2;    // K blocks of the second operand pair (classic kernel only)
+    float* rowmax; int64_t n_valid;   // classic kernel: per-row max of each tile's columns < n_valid
     void* C; int64_t c_ldm, c_ldz;
     int* err;
 };
@@ -268,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
             }
         }
         if (ok) {
+            float rmax = -__int_as_float(0x7f800000);
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 if (nkb > 0) {
@@ -289,6 +291,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                             o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
                         }
                         d[e] = o;
+                        if (r.rowmax) {
+                            const float f[4] = {o.x, o.y, o.z, o.w};
+                            for (int h = 0; h < 4; ++h)
+                                if (n + 4 * e + h < r.n_valid) rmax = fmaxf(rmax, f[h]);
+                        }
                     }
                 } else {
                     uint4* d = reinterpret_cast<uint4*>(static_cast<T*>(r.C) + off);
@@ -307,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                     }
                 }
             }
+            if (r.rowmax && m < r.M) r.rowmax[(int64_t(z) * r.M + m) * gridDim.x + blockIdx.x] = rmax;
         }
     }
     tc_fence_before();
@@ -524,7 +532,7 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
                         /*atom32=*/g.b_mn && sizeof(T) == 4))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
-          g.c_is_t ? 1 : 0, 0, g.a_batch_outer ? 1 : 0, 0, g.C, g.c_ldm, g.c_ldz, g.err};
+          g.c_is_t ? 1 : 0, 0, g.a_batch_outer ? 1 : 0, 0, nullptr, 0, g.C, g.c_ldm, g.c_ldz, g.err};
     Units U{ceil_div(g.N, BN), ceil_div(g.M, 128), 0};
     U.total = U.nt * U.mt * g.Z;
     auto kern = tc_gemm_persist_kernel<T, BN>;
@@ -554,7 +562,7 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
           g.c_is_t ? 1 : 0, g.c_accum ? 1 : 0, g.a_batch_outer ? 1 : 0, g.K2 > 0 ? ceil_div(g.K2, BK) : 0,
-          g.C, g.c_ldm, g.c_ldz, g.err};
+          g.rowmax, g.rowmax ? g.n_valid : 0, g.C, g.c_ldm, g.c_ldz, g.err};
     auto kern = tc_gemm_kernel<T, BN, S3>;
     const size_t smem = smem_bytes<BN, S3>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -584,7 +592,7 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
         } else {
             if (g.split3) return set_error(MLA_ERR_UNSUPPORTED, "MLA: 3xTF32 needs fp32 operands");
         }
-        if (!g.c_accum && g.K2 == 0 && !tc_gemm_classic()) {
+        if (!g.c_accum && g.K2 == 0 && !g.rowmax && !tc_gemm_classic()) {
             if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
             return tcg::launch_persist<T, 128>(g, st);
         }

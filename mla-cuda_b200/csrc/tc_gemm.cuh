@@ -35,6 +35,9 @@ struct TcGemm {
     const void* A2; int64_t a2_dims[3]; int64_t a2_ld[2];
     const void* B2; int64_t b2_dims[3]; int64_t b2_ld[2];
     int64_t K2;
+    // optional: rowmax[(z*M + m)*ntiles + tile] = max of row m over the tile's
+    // columns n < n_valid (fp32 output; ntiles = ceil(N / bn))
+    float* rowmax; int64_t n_valid;
     int* err;        // device error word (bounded waits)
 };
 
