@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-stages", action="store_true", help="skip the per-stage / per-precision timings")
     ap.add_argument("--shard", default=None, choices=["batch", "keys"],
                     help="multi-GPU layout: batch (weak scaling, default) or keys (strong scaling, default for c2)")
+    ap.add_argument("--qprep", default="redundant", choices=["heads", "redundant"],
+                    help="key sharding: Q-prep repeated on every rank (default), or sharded by heads + all-gather of q")
     return ap.parse_args()
 
 
@@ -139,12 +141,18 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-KEY_SHARDED = {"on": False}
+KEY_SHARDED = {"on": False, "heads": False}
 
 
 def run_forward(mcc, t, w, precision):
-    qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
-                               w.nope, w.rope, mc.EPS, precision=precision)
+    if KEY_SHARDED["heads"]:
+        # each rank holds its heads' slices of W_q_b / W_uk: local Q-prep, all-gather of q
+        from mla_custom_cuda import sharding
+        qa, qr = sharding.head_sharded_q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
+                                                  t["positions"], w.nope, w.rope, mc.EPS, precision=precision)
+    else:
+        qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                                   w.nope, w.rope, mc.EPS, precision=precision)
     if KEY_SHARDED["on"]:
         # every rank holds all sequences' queries and its own key slice; partial
         # attention, NCCL all-gather of (out, lse), exact log-sum-exp merge
@@ -238,6 +246,9 @@ def main_ours(args):
         t["c_kv"] = t["c_kv"][:, k0:k1].contiguous()
         t["pe_cache"] = t["pe_cache"][:, k0:k1].contiguous()
         KEY_SHARDED["on"] = True
+        if args.qprep == "heads" and w.heads % world == 0:
+            t["W_q_b"], t["W_uk"] = sharding.shard_q_weights(t["W_q_b"], t["W_uk"], w.nope, w.rope, rank, world)
+            KEY_SHARDED["heads"] = True
     else:
         t = mc.make_inputs(w, device=dev, gen="device", seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
@@ -265,11 +276,20 @@ def main_ours(args):
     with ClockSampler(local) as clk:
         t_w = time.perf_counter()
         n_w = 0
-        while n_w < max(args.warmup, 3) or time.perf_counter() - t_w < args.min_warmup_s:
+        while True:
             run_forward(mcc, t, w, precision)
             n_w += 1
             if n_w % 8 == 0:
                 torch.cuda.synchronize()
+            done = n_w >= max(args.warmup, 3) and time.perf_counter() - t_w >= args.min_warmup_s
+            if world > 1:
+                # every rank runs the same number of warm-up steps (a key-sharded step
+                # holds collectives)
+                flag = torch.tensor([0 if done else 1], device=dev, dtype=torch.int32)
+                torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MAX)
+                done = int(flag.item()) == 0
+            if done:
+                break
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
@@ -292,10 +312,18 @@ def main_ours(args):
     n_att = max(5, args.steps)
     stages = {}
     for prec in ((precision,) if args.no_stages else ("tensor", "exact")):
-        qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
-                                   w.nope, w.rope, mc.EPS, precision=prec)
-        att = timed(lambda: mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
-                                                 causal=w.causal, precision=prec), n_att)
+        if KEY_SHARDED["heads"]:
+            # local stages of a rank: Q-prep of its heads, attention over its key shard
+            from mla_custom_cuda import sharding
+            qa, qr = sharding.head_sharded_q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
+                                                      t["positions"], w.nope, w.rope, mc.EPS, precision=prec)
+            att = timed(lambda: mcc.mla_attention_partial(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
+                                                          precision=prec), n_att)
+        else:
+            qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                                       w.nope, w.rope, mc.EPS, precision=prec)
+            att = timed(lambda: mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
+                                                     causal=w.causal, precision=prec), n_att)
         qp = timed(lambda: mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
                                              t["positions"], w.nope, w.rope, mc.EPS, precision=prec), n_att)
         fwd = att + qp if prec != precision else ms
@@ -360,7 +388,7 @@ def main_ours(args):
                      + dtype_name + " storage",
             "data": "synthetic (seeded N(0,1) cache / activations, N(0,0.02) weights)",
             "config": {**w.describe(), "global_batch": B * (world if shard == "batch" else 1), "precision": precision,
-                       "parallelism": f"batch-shard dp{world}" if shard == "batch" else f"key-shard sp{world} (NCCL all-gather + LSE merge)",
+                       "parallelism": f"batch-shard dp{world}" if shard == "batch" else (f"key-shard sp{world} (NCCL all-gather + LSE merge)" + (", Q-prep head-sharded + all-gather of q" if KEY_SHARDED["heads"] else "")),
                        "l2": "inputs larger than L2 (cache %.2f GB per GPU)" % (cache_b / 1e9)},
             "stages": stages,
             "roofline": {"bound": "hbm", "kernel": "mla_attention (cache read)",

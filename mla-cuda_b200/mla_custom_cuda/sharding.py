@@ -8,6 +8,12 @@
   runs the attention on it (mla_attention_partial), all-gathers the partial
   outputs and their log-sum-exp over NCCL, and merges them with lse_combine.
   The merge is exact; the message per rank is B*Sq*H*(V + 1) values.
+* Head-sharded Q-prep (`head_shard`, `shard_q_weights`, `head_sharded_q_absorbed`)
+  for the key-sharded layout: Q-prep streams its weights on every GPU whatever
+  the key shard, so at long context and small batch it caps the scaling. Each
+  rank keeps only its heads' slices of W_q_b and W_uk, computes q for those
+  heads (2a1 and the RMSNorm are repeated on every rank) and the ranks
+  all-gather q (B*Sq*H*(kv_rank + rope) values) before the attention.
 
 The reference implementation is single-GPU; this module has no counterpart there.
 """
@@ -37,14 +43,71 @@ def key_shard(sk: int, rank: int, world: int) -> Tuple[int, int]:
     return _split(sk, rank, world)
 
 
-def gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """All-gather every rank's partial (out, lse) into [world, ...] tensors (rank order)."""
+def head_shard(heads: int, rank: int, world: int) -> Tuple[int, int]:
+    """Contiguous [start, end) of the heads whose queries `rank` computes."""
+    return _split(heads, rank, world)
+
+
+def shard_q_weights(W_q_b: torch.Tensor, W_uk: torch.Tensor, nope_dim: int, rope_dim: int, rank: int,
+                    world: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """This rank's heads of W_q_b [q_lora, H*(nope+rope)] and W_uk [H, nope, kv_rank],
+    as contiguous tensors (done once, at weight-load time)."""
+    heads = W_uk.shape[0]
+    if heads % world:
+        raise ValueError(f"{heads} heads do not split evenly over {world} ranks")
+    h0, h1 = head_shard(heads, rank, world)
+    qk = nope_dim + rope_dim
+    return W_q_b[:, h0 * qk:h1 * qk].contiguous(), W_uk[h0:h1].contiguous()
+
+
+def gather_heads(q_locals, group=None):
+    """All-gather per-rank [B, Sq, H/world, d_i] tensors into [B, Sq, H, d_i] (heads
+    in rank order), all of them in one collective."""
     world = dist.get_world_size(group)
-    outs = [torch.empty_like(out) for _ in range(world)]
-    lses = [torch.empty_like(lse) for _ in range(world)]
-    dist.all_gather(outs, out.contiguous(), group=group)
-    dist.all_gather(lses, lse.contiguous(), group=group)
-    return torch.stack(outs), torch.stack(lses)
+    flat = torch.cat([q.reshape(-1) for q in q_locals])
+    out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
+    if world == 1:
+        out.copy_(flat)
+    else:
+        dist.all_gather_into_tensor(out, flat, group=group)
+    out = out.view(world, -1)
+    res, off = [], 0
+    for q in q_locals:
+        n = q.numel()
+        B, Sq, Hl, d = q.shape
+        part = out[:, off:off + n].view(world, B, Sq, Hl, d)          # [rank, B, Sq, Hl, d]
+        res.append(part.permute(1, 2, 0, 3, 4).reshape(B, Sq, world * Hl, d))
+        off += n
+    return res
+
+
+def head_sharded_q_absorbed(x, W_q_a, q_norm_w, W_q_b_local, W_uk_local, positions, nope_dim: int, rope_dim: int,
+                            eps: float, group=None, precision: Optional[str] = None):
+    """q_absorbed / q_rope of all heads from each rank's head slices of the weights
+    (shard_q_weights): local Q-prep for H/world heads, then one all-gather of q."""
+    import mla_custom_cuda as mcc
+    qa, qr = mcc.q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b_local, W_uk_local, positions, nope_dim, rope_dim, eps,
+                               precision=precision)
+    qa_all, qr_all = gather_heads([qa, qr], group)
+    return qa_all, qr_all
+
+
+def gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """All-gather every rank's partial (out, lse) into [world, ...] tensors (rank
+    order), both in one collective (lse travels in out's dtype when that is fp32 or fp64)."""
+    world = dist.get_world_size(group)
+    if out.dtype != lse.dtype:   # 16-bit outputs: two collectives keep lse in fp32
+        outs = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=out.device)
+        lses = torch.empty((world,) + tuple(lse.shape), dtype=lse.dtype, device=lse.device)
+        dist.all_gather_into_tensor(outs, out.contiguous(), group=group)
+        dist.all_gather_into_tensor(lses, lse.contiguous(), group=group)
+        return outs, lses
+    flat = torch.cat([out.reshape(-1), lse.reshape(-1)])
+    buf = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(buf, flat, group=group)
+    buf = buf.view(world, -1)
+    n = out.numel()
+    return buf[:, :n].reshape((world,) + tuple(out.shape)), buf[:, n:].reshape((world,) + tuple(lse.shape))
 
 
 def sk_sharded_attention(q_absorbed, q_rope, c_kv_local, pe_local, W_uv, scale: float, group=None,

@@ -45,6 +45,47 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
+def _heads_worker(rank, world, port, result_q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import mla_configs as mc
+        from mla_custom_cuda import sharding
+        from oracle import mla_oracle as orc
+        small = mc.Workload("small", 3, 2, 19, hidden=96, heads=4, q_lora=48, kv_rank=32, nope=16, rope=8, v_dim=24)
+        t = {k: (v.double() if v.is_floating_point() else v) for k, v in mc.make_inputs(small, seed=3).items()}
+        Wqb_l, Wuk_l = sharding.shard_q_weights(t["W_q_b"], t["W_uk"], 16, 8, rank, world)
+        qa_l, qr_l = orc.q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], Wqb_l, Wuk_l, t["positions"], 16, 8)
+        qa, qr = sharding.gather_heads([qa_l, qr_l])
+        ra, rr = orc.q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"], 16, 8)
+        result_q.put((rank, rel_l2(qa, ra), rel_l2(qr, rr)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_head_sharded_q_prep_on_gloo(world):
+    """Each rank's head slices of W_q_b / W_uk give its heads' queries, and the
+    all-gather reassembles the full q in head order (oracle as the per-rank Q-prep)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_heads_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get() for _ in range(world))
+    for rank, e_a, e_r in res:
+        assert e_a < 1e-14 and e_r < 1e-14, (rank, e_a, e_r)
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_key_sharded_merge_on_gloo(world):
     ctx = mp.get_context("spawn")
