@@ -200,6 +200,29 @@ struct Bars {
     int abort;
 };
 
+// P.V of tile i: O += P(i) . V(i) (M = 128 heads, N = 256 latent dims, K = 32 keys),
+// A = P from TMEM, B = the key tile's latent half, MN-major, 128B swizzle (LBO =
+// stride between 64-dim chunks, SBO = stride between 8-key groups). Releases the
+// slot and signals o_done. Out of line: the MMA thread issues it from three places.
+template <int kSlots>
+__device__ __noinline__ bool issue_pv_mma(Bars* bars, uint32_t tmem, uint32_t smem_slots, int64_t i, bool first,
+                                          volatile int* abort, int* err, uint32_t idesc_o) {
+    const int sb = int(i % kSBufs);
+    if (!mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, err, ERR_TIMEOUT_BASE + 3)) return false;
+    tc_fence_after();
+    const int sl = int(i % kSlots);
+    const uint32_t base = smem_slots + sl * kSlotBytes;
+    const uint32_t p_tmem = tmem + kTmemS + sb * NK;
+    const uint64_t vd0 = smem_desc(base, kChunkBytes, 1024, 2);
+#pragma unroll
+    for (int k = 0; k < NK / 16; ++k)
+        mma_ts(tmem + kTmemO, p_tmem + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4), idesc_o,
+               (first && k == 0) ? 0u : 1u);
+    mma_commit(&bars->bf_empty[sl]);
+    mma_commit(&bars->o_done[sb]);
+    return true;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tm_ckv, const __grid_constant__ CUtensorMap tm_pe, const Params p)
@@ -301,30 +324,19 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 bool ok = true;
                 bool first_ring[kSBufs] = {true, true, true};
                 auto issue_pv = [&](int64_t i, bool first) -> bool {
-                    const int sb = int(i % kSBufs);
-                    if (!MLA_TW(2, mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
-                                             ERR_TIMEOUT_BASE + 3)))
-                        return false;
-                    tc_fence_after();
-                    const int sl = int(i % Tr::kSlots);
-                    const uint32_t base = smem_slots + sl * kSlotBytes;
-                    const uint32_t p_tmem = tmem + kTmemS + sb * NK;
-                    MLA_PROF(const long long tpv = clock64();)
-                    // B = V [16 keys x 256 latent], MN-major, 128B swizzle:
-                    // LBO = stride between 64-dim chunks, SBO = stride between 8-key groups.
-                    const uint64_t vd0 = smem_desc(base, kChunkBytes, 1024, 2);
-#pragma unroll
-                    for (int k = 0; k < NK / 16; ++k)
-                        mma_ts(tmem + kTmemO, p_tmem + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4), idesc_o,
-                               (first && k == 0) ? 0u : 1u);
-                    mma_commit(&bars->bf_empty[sl]);
-                    mma_commit(&bars->o_done[sb]);
-                    MLA_PROF(wacc[16] += clock64() - tpv;)
-                    return true;
+                    return issue_pv_mma<Tr::kSlots>(bars, tmem, smem_slots, i, first, abort, p.err, idesc_o);
                 };
+                int64_t pv_done = 0;   // P.V issued for tiles [0, pv_done)
                 for (int64_t i = 0; i < n && ok; ++i) {
                     const bool first = (i == 0) || it.j == 0;
                     if (first) {
+                        // Before waiting for this segment's query, issue the pending P.V up
+                        // to tile i-2: the softmax may be waiting for one of them (the
+                        // epilogue of a one-tile segment i-2, a rescale) before it loads
+                        // the query. P.V of tile i-1 stays behind: its softmax follows the
+                        // query load.
+                        for (; ok && pv_done < i - 1; ++pv_done) ok = issue_pv(pv_done, first_ring[pv_done % kSBufs]);
+                        if (!ok) break;
                         if (!MLA_TW(3, mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)))
                             break;
                         ++seg;
@@ -358,10 +370,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     MLA_PROF(wacc[17] += clock64() - tsi;)
                     trace_put(p, 1, i * 16 + 2);
                     first_ring[i % kSBufs] = first;
-                    if (i >= 2) ok = issue_pv(i - 2, first_ring[(i - 2) % kSBufs]);
+                    if (i >= 2 && pv_done == i - 2) {   // P.V trails the score MMA by two tiles
+                        ok = issue_pv(i - 2, first_ring[(i - 2) % kSBufs]);
+                        pv_done = i - 1;
+                    }
                     advance(p, it);
                 }
-                for (int64_t i = (n >= 2 ? n - 2 : 0); ok && i < n; ++i) ok = issue_pv(i, first_ring[i % kSBufs]);
+                for (; ok && pv_done < n; ++pv_done) ok = issue_pv(pv_done, first_ring[pv_done % kSBufs]);
             }
         } else if (warp >= 4 && warp < 8) {
             // ------------------------------------------------------------ softmax
