@@ -184,41 +184,35 @@ __global__ void __launch_bounds__(256) rope_gather_kernel(
 // each thread owning up to kVec float4 pieces of the row, all split-K partial loads
 // of a piece issued together. Same sums, in the same order, as lat_norm_kernel.
 template <typename T>
-__global__ void __launch_bounds__(256) lat_norm_vec_kernel(
+__global__ void __launch_bounds__(1024) lat_norm_vec_kernel(
     const float* __restrict__ P1, int splits, const T* __restrict__ gain,
     T* __restrict__ q_lat, int64_t M, int64_t q_lora, float eps)
 {
-    constexpr int kVec = 2;                       // q_lora <= 2048
+    constexpr int kMaxSplits = 16;                 // all split loads of a piece in flight at once
     const int64_t m = blockIdx.x;
     const int n4 = int(q_lora / 4);
-    float4 v[kVec];
-    float ss = 0.f;
+    const int c = threadIdx.x;                     // one float4 piece of the row per thread
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (c < n4) {
+        float4 t[kMaxSplits];
 #pragma unroll
-    for (int e = 0; e < kVec; ++e) {
-        const int c = threadIdx.x + e * 256;
-        v[e] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (c < n4) {
-            for (int z = 0; z < splits; ++z) {
-                const float4 t = __ldg(reinterpret_cast<const float4*>(P1 + (int64_t(z) * M + m) * q_lora) + c);
-                v[e].x += t.x; v[e].y += t.y; v[e].z += t.z; v[e].w += t.w;
-            }
-        }
-        ss = fmaf(v[e].x, v[e].x, ss); ss = fmaf(v[e].y, v[e].y, ss);
-        ss = fmaf(v[e].z, v[e].z, ss); ss = fmaf(v[e].w, v[e].w, ss);
+        for (int z = 0; z < kMaxSplits; ++z)
+            if (z < splits) t[z] = __ldg(reinterpret_cast<const float4*>(P1 + (int64_t(z) * M + m) * q_lora) + c);
+#pragma unroll
+        for (int z = 0; z < kMaxSplits; ++z)
+            if (z < splits) { v.x += t[z].x; v.y += t[z].y; v.z += t[z].z; v.w += t[z].w; }
     }
-    __shared__ float red[8];
+    float ss = v.x * v.x;
+    ss = fmaf(v.y, v.y, ss); ss = fmaf(v.z, v.z, ss); ss = fmaf(v.w, v.w, ss);
+    __shared__ float red[32];
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) t += red[w];
-    const float inv_rms = 1.f / sqrtf(t / float(q_lora) + eps);
-#pragma unroll
-    for (int e = 0; e < kVec; ++e) {
-        const int c = threadIdx.x + e * 256;
-        if (c >= n4) continue;
-        const float f[4] = {v[e].x, v[e].y, v[e].z, v[e].w};
+    float tot = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) tot += red[w];
+    const float inv_rms = 1.f / sqrtf(tot / float(q_lora) + eps);
+    if (c < n4) {
+        const float f[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k)
             q_lat[m * q_lora + 4 * c + k] = cvt<T>(f[k] * inv_rms * cvt<float>(gain[4 * c + k]));
@@ -229,8 +223,9 @@ template <typename T>
 mla_status_t launch_lat_norm(const acc_t<T>* P1, int splits, const T* gain, T* q_lat, int64_t M, int64_t q_lora,
                              double eps, cudaStream_t st) {
     if constexpr (std::is_same<acc_t<T>, float>::value) {
-        if (q_lora % 4 == 0 && q_lora <= 2048) {
-            lat_norm_vec_kernel<T><<<unsigned(M), 256, 0, st>>>(P1, splits, gain, q_lat, M, q_lora, float(eps));
+        if (q_lora % 4 == 0 && q_lora <= 4096 && splits <= 16) {
+            const unsigned threads = unsigned((q_lora / 4 + 31) / 32 * 32);
+            lat_norm_vec_kernel<T><<<unsigned(M), threads, 0, st>>>(P1, splits, gain, q_lat, M, q_lora, float(eps));
             return check_launch("q latent RMSNorm (2a-norm)");
         }
     }
@@ -252,7 +247,8 @@ __device__ __forceinline__ void store4(NopeT* dst, float a, float b, float c, fl
 template <typename T, typename NopeT>
 __global__ void __launch_bounds__(256) rope_gather_vec_kernel(
     const float* __restrict__ P2, int splits, NopeT* __restrict__ q_nope, T* __restrict__ q_rope,
-    int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, const float* __restrict__ cs)
+    int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope, const int64_t* __restrict__ positions,
+    const RopeTable<T> tab)
 {
     const int lane = threadIdx.x & 31;
     const int64_t qk = nope + rope;
@@ -275,11 +271,15 @@ __global__ void __launch_bounds__(256) rope_gather_vec_kernel(
             const float4 v = sum4(c);
             store4<NopeT>(q_nope + mh * nope + c, v.x, v.y, v.z, v.w);
         }
-        const float* t = cs + 2 * ((m % sq) * (rope / 2));
+        const float pos = float(positions[m % sq]);
         for (int64_t c = 4 * lane; c < rope; c += 128) {
             const float4 v = sum4(nope + c);                   // pairs j = c/2 and c/2 + 1
             const int64_t j = c / 2;
-            const float c0 = t[2 * j], s0 = t[2 * j + 1], c1 = t[2 * j + 2], s1 = t[2 * j + 3];
+            // cos / sin in the accumulate dtype narrowed to the storage dtype, as
+            // rope_table_kernel computes them
+            const float a0 = pos * tab.inv_freq[j], a1 = pos * tab.inv_freq[j + 1];
+            const float c0 = cvt<float>(cvt<T>(cos(a0))), s0 = cvt<float>(cvt<T>(sin(a0)));
+            const float c1 = cvt<float>(cvt<T>(cos(a1))), s1 = cvt<float>(cvt<T>(sin(a1)));
             T* o = q_rope + mh * rope + c;
             o[0] = cvt<T>(v.x * c0 - v.y * s0);
             o[1] = cvt<T>(v.x * s0 + v.y * c0);
@@ -289,19 +289,24 @@ __global__ void __launch_bounds__(256) rope_gather_vec_kernel(
     }
 }
 
+// 2b launcher. The vectorised kernel computes its cos / sin inline; the generic
+// one reads them from a table (cs, in the workspace) filled first.
 template <typename T, typename NopeT>
 mla_status_t launch_rope_gather(const acc_t<T>* P2, int splits, const int64_t* positions, NopeT* q_nope, T* q_rope,
                                 int64_t M, int64_t sq, int64_t heads, int64_t nope, int64_t rope,
-                                const acc_t<T>* cs, cudaStream_t st) {
+                                const RopeTable<T>& tab, acc_t<T>* cs, cudaStream_t st) {
     if constexpr (std::is_same<acc_t<T>, float>::value) {
         if (nope % 4 == 0 && rope % 4 == 0) {
             int64_t blocks = ceil_div(M * heads, 8);
             if (blocks > 32LL * sm_count()) blocks = 32LL * sm_count();
             rope_gather_vec_kernel<T, NopeT><<<unsigned(blocks), 256, 0, st>>>(P2, splits, q_nope, q_rope, M, sq,
-                                                                             heads, nope, rope, cs);
+                                                                             heads, nope, rope, positions, tab);
             return check_launch("q rope (2b)");
         }
     }
+    const int64_t tblocks = ceil_div(sq * (rope / 2), 256);
+    rope_table_kernel<T><<<unsigned(tblocks > 0 ? tblocks : 1), 256, 0, st>>>(positions, sq, rope / 2, tab, cs);
+    MLA_TRY(check_launch("q rope table"));
     const int64_t total = M * heads * (nope + rope / 2);
     int64_t blocks = ceil_div(total, 256);
     const int64_t cap = 16LL * sm_count();
@@ -472,11 +477,8 @@ mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
     }
     {
         Acc* cs = reinterpret_cast<Acc*>(ws + p.off_cs);
-        const int64_t tblocks = ceil_div(a.sq * (a.rope / 2), 256);
-        rope_table_kernel<T><<<unsigned(tblocks > 0 ? tblocks : 1), 256, 0, st>>>(a.positions, a.sq, a.rope / 2, tab, cs);
-        MLA_TRY(check_launch("q rope table"));
         MLA_TRY((launch_rope_gather<T, Acc>(P2, p.split2, a.positions, q_nope, static_cast<T*>(a.q_rope), M, a.sq,
-                                            a.heads, a.nope, a.rope, cs, st)));
+                                            a.heads, a.nope, a.rope, tab, cs, st)));
     }
     if (p.small) {
         MLA_TRY((launch_absorb<CfgSmall<Acc>, T>(q_nope, static_cast<const T*>(a.W_uk),
@@ -603,11 +605,8 @@ mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3) {
         // q_nope in the storage dtype: the left operand of the 2c tensor-core GEMM,
         // whose operands share one dtype
         Acc* cs = reinterpret_cast<Acc*>(ws + p.off_cs);
-        const int64_t tblocks = ceil_div(a.sq * (a.rope / 2), 256);
-        rope_table_kernel<T><<<unsigned(tblocks > 0 ? tblocks : 1), 256, 0, st>>>(a.positions, a.sq, a.rope / 2, tab, cs);
-        MLA_TRY(check_launch("q rope table"));
         MLA_TRY((launch_rope_gather<T, T>(P2, p.split2, a.positions, q_nope_t, static_cast<T*>(a.q_rope), M, a.sq,
-                                          a.heads, a.nope, a.rope, cs, st)));
+                                          a.heads, a.nope, a.rope, tab, cs, st)));
     }
     TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h]
     g3.A = q_nope_t; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;
