@@ -31,7 +31,7 @@ enum : int { ERR_TIMEOUT_BASE = 200 };
 
 struct Run {
     int64_t M, N, K, k_chunk;
-    int Z, spb, b_mn, c_is_t, c_accum, a_batch_outer;
+    int Z, spb, b_mn, c_is_t;
     int64_t nkb2;    // K blocks of the second operand pair (classic kernel only)
     float* rowmax; int64_t n_valid;   // classic kernel: per-row max of each tile's columns < n_valid
     void* C; int64_t c_ldm, c_ldz;
@@ -131,8 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
             const int32_t k = second ? int32_t((i - nkb1) * BK) : int32_t(kb + i * BK);
             unsigned char* st = smem + s * kStage;
             mbar_arrive_expect_tx(&full[s], uint32_t(kStage));
-            if (r.a_batch_outer) tma_load_3d(st, ma, &full[s], k, int32_t(m0), ya);
-            else tma_load_3d(st, ma, &full[s], k, ya, int32_t(m0));
+            tma_load_3d(st, ma, &full[s], k, ya, int32_t(m0));
             unsigned char* bdst = st + a_bytes();
             if (r.b_mn) {
                 for (int g = 0; g < BN / BK; ++g)   // BK-wide column groups of N, BK rows of K each
@@ -286,10 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                     for (int e = 0; e < 8; ++e) {
                         float4 o = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
                                                __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
-                        if (r.c_accum) {
-                            const float4 prev = d[e];
-                            o.x += prev.x; o.y += prev.y; o.z += prev.z; o.w += prev.w;
-                        }
                         d[e] = o;
                         if (r.rowmax) {
                             const float f[4] = {o.x, o.y, o.z, o.w};
@@ -410,8 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
                 const int32_t k = int32_t(kb + i * BK);
                 unsigned char* st = smem + s * kStage;
                 mbar_arrive_expect_tx(&full[s], uint32_t(kStage));
-                if (r.a_batch_outer) tma_load_3d(st, &tmA, &full[s], k, int32_t(m0), ya);
-                else tma_load_3d(st, &tmA, &full[s], k, ya, int32_t(m0));
+                tma_load_3d(st, &tmA, &full[s], k, ya, int32_t(m0));
                 unsigned char* bdst = st + a_bytes();
                 if (r.b_mn) {
                     for (int g = 0; g < BN / BK; ++g)
@@ -524,7 +518,7 @@ template <typename T, int BN>
 mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
     constexpr int BK = tc_gemm_bk<T>();
     CUtensorMap ta, tb;
-    const uint32_t abox[3] = {uint32_t(BK), g.a_batch_outer ? 128u : 1u, g.a_batch_outer ? 1u : 128u};
+    const uint32_t abox[3] = {uint32_t(BK), 1u, 128u};
     const uint32_t bbox_mn[3] = {uint32_t(BK), uint32_t(BK), 1u};
     const uint32_t bbox_k[3] = {uint32_t(BK), uint32_t(BN), 1u};
     if (!make_map_3d<T>(&ta, g.A, g.a_dims, g.a_ld, abox, true) ||
@@ -532,7 +526,7 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
                         /*atom32=*/g.b_mn && sizeof(T) == 4))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
-          g.c_is_t ? 1 : 0, 0, g.a_batch_outer ? 1 : 0, 0, nullptr, 0, g.C, g.c_ldm, g.c_ldz, g.err};
+          g.c_is_t ? 1 : 0, 0, nullptr, 0, g.C, g.c_ldm, g.c_ldz, g.err};
     Units U{ceil_div(g.N, BN), ceil_div(g.M, 128), 0};
     U.total = U.nt * U.mt * g.Z;
     auto kern = tc_gemm_persist_kernel<T, BN>;
@@ -547,7 +541,7 @@ template <typename T, int BN, bool S3>
 mla_status_t launch(const TcGemm& g, cudaStream_t st) {
     constexpr int BK = tc_gemm_bk<T>();
     CUtensorMap ta, tb;
-    const uint32_t abox[3] = {uint32_t(BK), g.a_batch_outer ? 128u : 1u, g.a_batch_outer ? 1u : 128u};
+    const uint32_t abox[3] = {uint32_t(BK), 1u, 128u};
     const uint32_t bbox_mn[3] = {uint32_t(BK), uint32_t(BK), 1u};
     const uint32_t bbox_k[3] = {uint32_t(BK), uint32_t(BN), 1u};
     if (!make_map_3d<T>(&ta, g.A, g.a_dims, g.a_ld, abox, true) ||
@@ -561,7 +555,7 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
                          /*atom32=*/g.b_mn && sizeof(T) == 4)))
         return set_error(MLA_ERR_CUDA, "MLA: tensor map for the tensor-core GEMM failed (alignment?)");
     Run r{g.M, g.N, g.K, g.spb > 1 ? g.k_chunk : g.K, g.Z, g.spb > 1 ? g.spb : 1, g.b_mn ? 1 : 0,
-          g.c_is_t ? 1 : 0, g.c_accum ? 1 : 0, g.a_batch_outer ? 1 : 0, g.K2 > 0 ? ceil_div(g.K2, BK) : 0,
+          g.c_is_t ? 1 : 0, g.K2 > 0 ? ceil_div(g.K2, BK) : 0,
           g.rowmax, g.rowmax ? g.n_valid : 0, g.C, g.c_ldm, g.c_ldz, g.err};
     auto kern = tc_gemm_kernel<T, BN, S3>;
     const size_t smem = smem_bytes<BN, S3>();
@@ -592,7 +586,7 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
         } else {
             if (g.split3) return set_error(MLA_ERR_UNSUPPORTED, "MLA: 3xTF32 needs fp32 operands");
         }
-        if (!g.c_accum && g.K2 == 0 && !g.rowmax && !tc_gemm_classic()) {
+        if (g.K2 == 0 && !g.rowmax && !tc_gemm_classic()) {
             if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
             return tcg::launch_persist<T, 128>(g, st);
         }

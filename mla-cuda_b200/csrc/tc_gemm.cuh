@@ -9,25 +9,24 @@ namespace mla {
 // C[z][m][n] = sum_k A[z][m][k] * B[z][k][n], accumulated in fp32 on the tensor
 // cores (kind::tf32 for fp32 operands, kind::f16 for bf16 / fp16).
 //   A : 3-D tensor, element (k, y, m) at k + y*a_ld[0] + m*a_ld[1] with dims
-//       {K, Ay, M}; or, with a_batch_outer, element (k, m, y) at
-//       k + m*a_ld[0] + y*a_ld[1] with dims {K, M, Ay}. y is the batch.
+//       {K, Ay, M}; y is the batch.
 //   B : MN-major {N, K, Bz}: element (n, k, z) at n + k*b_ld[0] + z*b_ld[1]
 //       (a row-major [K][N] weight), or K-major {K, N, Bz}: (k, n, z) at
 //       k + n*b_ld[0] + z*b_ld[1] (a row-major [N][K] weight).
 //   Z launches = batches x spb: launch z works on batch z / spb and on K slice
 //       z % spb (k_chunk elements, a multiple of the K block; spb = 1: all of K).
 //   C : element (m, n) of launch z at c + m*c_ldm + z*c_ldz + n, stored as fp32
-//       or as the storage dtype (c_is_t); c_accum adds to what C holds (fp32).
+//       or as the storage dtype (c_is_t).
 //   split3 (fp32 only): 3xTF32 — each operand is split into a tf32 head and an
 //       fp32 remainder and A*B is accumulated as hi*hi + hi*lo + lo*hi, which
 //       keeps products to about 2^-21 relative (fp32-class accuracy) at a third
 //       of the tf32 rate.
 struct TcGemm {
-    const void* A; int64_t a_dims[3]; int64_t a_ld[2]; bool a_batch_outer;
+    const void* A; int64_t a_dims[3]; int64_t a_ld[2];
     const void* B; bool b_mn; int64_t b_dims[3]; int64_t b_ld[2];
     int64_t M, N, K;
     int Z; int spb; int64_t k_chunk;
-    void* C; bool c_is_t; bool c_accum; int64_t c_ldm, c_ldz;
+    void* C; bool c_is_t; int64_t c_ldm, c_ldz;
     int bn;          // 128 or 256 output columns per CTA
     bool split3;
     // optional second operand pair, accumulated after A*B: C += A2*B2 over K2
