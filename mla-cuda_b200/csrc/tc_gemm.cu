@@ -22,6 +22,9 @@ namespace tcg {
 using namespace sm100;
 
 constexpr int kThreads = 192;
+// 3xTF32 form of the one-tile kernel: warps 6-9 split the landed stages while
+// warps 2-5 drain the accumulator, so neither waits for the other
+template <bool S3> constexpr int kernel_threads() { return S3 ? 320 : kThreads; }
 // 3xTF32: K blocks (32 elements each) summed into one TMEM accumulator before it is
 // drained into the round-to-nearest running sum. Measured against fp64 on the
 // attention fixtures: 1 block per drain matches fp32 CPU accuracy (rel-L2 7e-7),
@@ -60,7 +63,7 @@ template <int BN, bool S3> constexpr size_t smem_bytes() {
 }
 
 template <typename T, int BN, bool S3>
-__global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
+__global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, const Run r)
 {
@@ -68,10 +71,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     constexpr int BK = tc_gemm_bk<T>();             // elements per 128-byte row
     constexpr int kInstK = 32 / int(sizeof(T));      // K per MMA instruction (32 bytes)
     constexpr int kStage = a_bytes() + b_bytes<BN>();
-    // 3xTF32: two accumulators of BN columns (ping-pong over groups of kGroup K blocks)
-    // and a running sum at 2*BN
+    // 3xTF32: two accumulators of BN columns (ping-pong over groups of kGroup K blocks),
+    // a running sum at 2*BN, and two slots of the split A operand (tf32 hi | lo, one
+    // 32-wide K block each: 64 columns) at kTmemA, read by ts-form MMAs
     constexpr uint32_t kTmemCols = S3 ? 512u : uint32_t(BN);
     static_assert(!S3 || BN == 128, "3xTF32 uses 128-column tiles");
+    constexpr uint32_t kTmemA = 3u * BN;                 // 384: 2 slots x (32 hi + 32 lo) columns
     static_assert(!S3 || std::is_same<T, float>::value, "3xTF32 needs fp32 operands");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -82,7 +87,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
     uint64_t* split_done = empty + S;
     uint64_t* acc_full = split_done + S;          // [2]: accumulator buffer ready (3xTF32 uses both)
     uint64_t* acc_empty = acc_full + 2;           // [2]: 3xTF32 accumulator drained into the sum
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* a_free = acc_empty + 2;             // [2]: 3xTF32 TMEM A slot read by its MMAs
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_free + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
     volatile int* abort = abort_flag;
 
@@ -105,6 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
         for (int i = 0; i < 2; ++i) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 128);
+            mbar_init(&a_free[i], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -157,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                                         ERR_TIMEOUT_BASE + 5)) { ok = false; break; }
             }
             tc_fence_after();
+            const uint32_t a_hi = tmem + kTmemA + uint32_t(i & 1) * 64u;   // 3xTF32: split A in TMEM
             const uint32_t a0 = smem_u32(smem + s * kStage);
             const uint32_t b0 = a0 + a_bytes();
             // B MN-major: column groups BK*128 bytes apart (LBO), K-row groups SBO apart:
@@ -173,10 +181,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                 const uint64_t bd = bd0 + uint64_t((r.b_mn ? kk * (kInstK * 128) : kk * 32) >> 4);
                 const uint32_t acc = (fresh && kk == 0) ? 0u : 1u;
                 if constexpr (std::is_same<T, float>::value) {
-                    if constexpr (S3) {   // small terms first
-                        mma_ss_tf32(d, ad, bd + lo_off, idesc, acc);     // hi * lo
-                        mma_ss_tf32(d, ad + lo_off, bd, idesc, 1u);      // lo * hi
-                        mma_ss_tf32(d, ad, bd, idesc, 1u);               // hi * hi
+                    if constexpr (S3) {   // small terms first; A halves from TMEM
+                        mma_ts_tf32(d, a_hi + kk * 8, bd + lo_off, idesc, acc);      // hi * lo
+                        mma_ts_tf32(d, a_hi + 32 + kk * 8, bd, idesc, 1u);           // lo * hi
+                        mma_ts_tf32(d, a_hi + kk * 8, bd, idesc, 1u);                // hi * hi
                     } else {
                         mma_ss_tf32(d, ad, bd, idesc, acc);
                     }
@@ -186,11 +194,67 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
             }
             mma_commit(&empty[s]);
             if constexpr (S3) {
+                mma_commit(&a_free[i & 1]);
                 if ((i + 1) % kGroup == 0 || i + 1 == nkb) mma_commit(&acc_full[(i / kGroup) & 1]);
             }
         }
         if (ok && !S3) mma_commit(acc_full);
-    } else if (warp >= 2) {
+    } else if (S3 && warp >= 6) {
+        // ------------------------------------------------------------ 3xTF32 split
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_off = uint32_t(q * 32) << 16;
+        const int ts = threadIdx.x - 192;
+        bool ok = true;
+        for (int64_t i = 0; i < nkb && ok; ++i) {
+            const int s = int(i % S);
+            ok = __all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t((i / S) & 1), abort, r.err,
+                                                   ERR_TIMEOUT_BASE + 4));
+            if (!ok) break;
+            // A: my row (= my TMEM lane) of the 32-wide K block, split into the
+            // TMEM slot of this block once its previous MMAs have read it
+            ok = __all_sync(0xffffffffu, mbar_wait(&a_free[i & 1], uint32_t(((i >> 1) & 1) ^ 1), abort, r.err,
+                                                   ERR_TIMEOUT_BASE + 7));
+            if (!ok) break;
+            tc_fence_after();
+            {
+                const unsigned char* arow = smem + s * kStage + row * 128;
+                uint32_t h[32], l[32];
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {   // 16-byte chunk c sits at c ^ (row % 8) (128B swizzle)
+                    const uint4 v = *reinterpret_cast<const uint4*>(arow + ((c ^ (row & 7)) << 4));
+                    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        h[4 * c + e] = tf32_rna(w[e]);
+                        l[4 * c + e] = tf32_rna(__float_as_uint(__uint_as_float(w[e]) - __uint_as_float(h[4 * c + e])));
+                    }
+                }
+                const uint32_t a_slot = tmem + lane_off + kTmemA + uint32_t(i & 1) * 64u;
+                tmem_st32(a_slot, h);
+                tmem_st32(a_slot + 32, l);
+            }
+            // B: hi in place, lo into the remainder buffer
+            uint4* x = reinterpret_cast<uint4*>(smem + s * kStage + a_bytes());
+            uint4* y = reinterpret_cast<uint4*>(lo + s * kStage + a_bytes());
+#pragma unroll 4
+            for (int e = ts; e < b_bytes<BN>() / 16; e += 128) {
+                uint4 v = x[e], h, l;
+                h.x = tf32_rna(v.x); h.y = tf32_rna(v.y); h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
+                l.x = __float_as_uint(__uint_as_float(v.x) - __uint_as_float(h.x));
+                l.y = __float_as_uint(__uint_as_float(v.y) - __uint_as_float(h.y));
+                l.z = __float_as_uint(__uint_as_float(v.z) - __uint_as_float(h.z));
+                l.w = __float_as_uint(__uint_as_float(v.w) - __uint_as_float(h.w));
+                l.x = tf32_rna(l.x); l.y = tf32_rna(l.y); l.z = tf32_rna(l.z); l.w = tf32_rna(l.w);
+                x[e] = h;
+                y[e] = l;
+            }
+            tmem_st_wait();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&split_done[s]);
+        }
+    } else if (warp >= 2 && warp < 6) {
         const int q = warp & 3;                       // TMEM lane quadrant of this warp
         const int row = q * 32 + lane;
         const int64_t m = m0 + row;
@@ -205,7 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
             // grows with the number of MMAs summed into one accumulator: every kGroup K
             // blocks the accumulator is drained into a running sum (fp32, round to
             // nearest) kept in TMEM columns [2*BN, 3*BN).
-            const int t = threadIdx.x - 64;
             const int64_t ngroups = (nkb + kGroup - 1) / kGroup;
             auto harvest = [&](int64_t gi) -> bool {
                 if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[gi & 1], uint32_t((gi >> 1) & 1), abort, r.err,
@@ -234,32 +297,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_kernel(
                 mbar_arrive(&acc_empty[gi & 1]);
                 return true;
             };
-            for (int64_t i = 0; i < nkb && ok; ++i) {
-                const int s = int(i % S);
-                ok = __all_sync(0xffffffffu, mbar_wait(&full[s], uint32_t((i / S) & 1), abort, r.err,
-                                                       ERR_TIMEOUT_BASE + 4));
-                if (!ok) break;
-                uint4* x = reinterpret_cast<uint4*>(smem + s * kStage);
-                uint4* y = reinterpret_cast<uint4*>(lo + s * kStage);
-#pragma unroll 4
-                for (int e = t; e < kStage / 16; e += 128) {
-                    uint4 v = x[e], h, l;
-                    h.x = tf32_rna(v.x); h.y = tf32_rna(v.y); h.z = tf32_rna(v.z); h.w = tf32_rna(v.w);
-                    l.x = __float_as_uint(__uint_as_float(v.x) - __uint_as_float(h.x));
-                    l.y = __float_as_uint(__uint_as_float(v.y) - __uint_as_float(h.y));
-                    l.z = __float_as_uint(__uint_as_float(v.z) - __uint_as_float(h.z));
-                    l.w = __float_as_uint(__uint_as_float(v.w) - __uint_as_float(h.w));
-                    l.x = tf32_rna(l.x); l.y = tf32_rna(l.y); l.z = tf32_rna(l.z); l.w = tf32_rna(l.w);
-                    x[e] = h;
-                    y[e] = l;
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(&split_done[s]);
-                // drain the previous group once this group's last block is handed over,
-                // so the MMAs of this group overlap the drain
-                if (((i + 1) % kGroup == 0 || i + 1 == nkb) && i / kGroup >= 1) ok = harvest(i / kGroup - 1);
-            }
-            if (ok && ngroups > 0) ok = harvest(ngroups - 1);
+
+            for (int64_t gi = 0; gi < ngroups && ok; ++gi) ok = harvest(gi);
+
             res = tmem + 2u * BN;
         } else {
             if (ok && nkb > 0) {
@@ -561,7 +601,7 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
     const size_t smem = smem_bytes<BN, S3>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     dim3 grid(unsigned(ceil_div(g.N, BN)), unsigned(ceil_div(g.M, 128)), unsigned(g.Z));
-    kern<<<grid, kThreads, smem, st>>>(ta, tb, ta2, tb2, r);
+    kern<<<grid, kernel_threads<S3>(), smem, st>>>(ta, tb, ta2, tb2, r);
     return check_launch("tensor-core GEMM");
 }
 
