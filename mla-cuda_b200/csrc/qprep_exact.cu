@@ -512,13 +512,24 @@ struct QTPlan {
     size_t off_err, off_p1, off_qlat, off_p2, off_qnope, off_cs, total;
 };
 
-int tc_split(int64_t tiles, int64_t K, int64_t bk, int waves, int64_t& chunk) {
-    const int64_t want = int64_t(waves) * sm_count();
-    int64_t s = want / (tiles > 0 ? tiles : 1);
+// Split-K plan of a weight-streaming GEMM (one CTA per SM): the slice count s
+// minimises (rounds of CTAs * SMs / units) + s * 2M/K, the time of the weight
+// stream relative to a perfectly balanced one plus the fp32 partials each slice
+// writes and the next kernel reads (M*N per slice against K*N weights); at
+// least four K blocks per slice.
+int tc_split(int64_t tiles, int64_t M, int64_t K, int64_t bk, int64_t& chunk) {
     const int64_t kblocks = ceil_div(K, bk);
-    if (s > kblocks / 4) s = kblocks / 4;     // at least four K blocks per slice
-    if (s < 1) s = 1;
-    const int64_t cb = ceil_div(kblocks, s);
+    const int64_t sms = sm_count();
+    int64_t best = 1;
+    double best_cost = 1e30;
+    for (int64_t s = 1; s <= 32 && s <= (kblocks / 4 > 1 ? kblocks / 4 : 1); ++s) {
+        const int64_t cb = ceil_div(kblocks, s);
+        const int64_t slices = ceil_div(kblocks, cb);            // non-empty slices
+        const int64_t units = tiles * slices;
+        const double cost = double(ceil_div(units, sms) * sms) / double(units) + double(slices) * 2.0 * double(M) / double(K);
+        if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
+    }
+    const int64_t cb = ceil_div(kblocks, best);
     chunk = cb * bk;
     return int(ceil_div(kblocks, cb));
 }
@@ -531,8 +542,8 @@ QTPlan make_tplan(const QArgs& a) {
     const int64_t ncols = a.heads * (a.nope + a.rope);
     const int64_t bk = tc_gemm_bk<T>();
     const int64_t mt = ceil_div(M, 128);
-    p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), a.hidden, bk, 1, p.chunk1);
-    p.split2 = tc_split(mt * ceil_div(ncols, 128), a.q_lora, bk, 1, p.chunk2);
+    p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), M, a.hidden, bk, p.chunk1);
+    p.split2 = tc_split(mt * ceil_div(ncols, 128), M, a.q_lora, bk, p.chunk2);
     size_t off = 0;
     p.off_err = off;   off = align_up(off + 256, 256);
     p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(Acc), 256);
