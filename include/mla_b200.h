@@ -60,9 +60,11 @@ typedef enum mla_dtype {
 } mla_dtype_t;
 
 /* Arithmetic used by a call.
- *  MLA_PREC_EXACT : every product and sum in the accumulate dtype (fp64 for
- *                   fp64 storage, fp32 otherwise), the reference's policy
- *                   (AccType, mla_kernels.cu:118-120). rel-L2 <= 1e-5 in fp32.
+ *  MLA_PREC_EXACT : the accuracy of the accumulate dtype (fp64 for fp64
+ *                   storage, fp32 otherwise), the reference's policy (AccType,
+ *                   mla_kernels.cu:118-120). fp32 storage runs the contractions
+ *                   on the tensor cores in 3xTF32 (fp32-class products, fp32
+ *                   sums); other dtypes on CUDA cores. rel-L2 <= 1e-5 in fp32.
  *  MLA_PREC_TENSOR: tcgen05 tensor cores with bf16 operands and fp32
  *                   accumulation, scores never written to memory. fp32, fp16
  *                   and bf16 storage; rel-L2 <= 2e-2 against the fp32 path. */

@@ -17,8 +17,9 @@ reference (mla_kernels.cu:664-667, :1528-1549).
 There is no CPU or PyTorch fallback: importing this module fails if the
 library is missing, and every call requires CUDA tensors.
 
-Precision: the default, ``"exact"``, computes in the accumulate dtype like the
-reference (fp64 for fp64 tensors, fp32 otherwise). ``"tensor"`` runs the
+Precision: the default, ``"exact"``, computes to the accuracy of the accumulate
+dtype like the reference (fp64 for fp64 tensors, fp32 otherwise; fp32 runs its
+contractions on the tensor cores in 3xTF32). ``"tensor"`` runs the
 tcgen05 tensor-core kernels (bf16 operands, fp32 accumulation) where they cover
 the shape. Select it with ``set_precision("tensor")``, the ``MLA_PRECISION``
 environment variable, or the ``precision=`` argument of the ``*_ex`` calls.
