@@ -97,11 +97,11 @@ def gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None) -> Tuple[t
     order), both in one collective (lse travels in out's dtype when that is fp32 or fp64)."""
     world = dist.get_world_size(group)
     if out.dtype != lse.dtype:   # 16-bit outputs: two collectives keep lse in fp32
-        outs = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device=out.device)
-        lses = torch.empty((world,) + tuple(lse.shape), dtype=lse.dtype, device=lse.device)
-        dist.all_gather_into_tensor(outs, out.contiguous(), group=group)
-        dist.all_gather_into_tensor(lses, lse.contiguous(), group=group)
-        return outs, lses
+        outs = torch.empty(world * out.numel(), dtype=out.dtype, device=out.device)
+        lses = torch.empty(world * lse.numel(), dtype=lse.dtype, device=lse.device)
+        dist.all_gather_into_tensor(outs, out.contiguous().reshape(-1), group=group)
+        dist.all_gather_into_tensor(lses, lse.contiguous().reshape(-1), group=group)
+        return outs.view((world,) + tuple(out.shape)), lses.view((world,) + tuple(lse.shape))
     flat = torch.cat([out.reshape(-1), lse.reshape(-1)])
     buf = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
     dist.all_gather_into_tensor(buf, flat, group=group)

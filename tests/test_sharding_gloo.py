@@ -113,3 +113,44 @@ def test_shard_ranges_cover_exactly():
         assert sharding.batch_shard(n, 0, world) == spans[0]
     with pytest.raises(ValueError):
         sharding.key_shard(10, 4, 4)
+
+
+def _partials_dtype_worker(rank, world, port, result_q):
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from mla_custom_cuda import sharding
+        g = torch.Generator().manual_seed(100 + rank)
+        ok = True
+        for out_dtype in (torch.float32, torch.float16):
+            out = torch.randn(2, 3, 4, 8, generator=g).to(out_dtype)
+            lse = torch.randn(2, 3, 4, generator=g)
+            outs, lses = sharding.gather_partials(out, lse)
+            # every rank's slice arrives in rank order, dtypes kept
+            mine_ok = torch.equal(outs[rank], out) and torch.equal(lses[rank], lse)
+            ok = ok and mine_ok and outs.dtype == out_dtype and lses.dtype == torch.float32
+            ok = ok and tuple(outs.shape) == (world, 2, 3, 4, 8) and tuple(lses.shape) == (world, 2, 3, 4)
+        result_q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_partials_keeps_rank_order_and_dtypes():
+    """One collective when out and lse share a dtype, two (lse kept in fp32) otherwise."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_partials_dtype_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = sorted(q.get() for _ in range(world))
+    assert all(ok for _, ok in res), res
