@@ -1,9 +1,9 @@
 """Generates tests/golden/*.npz from the reference's own PyTorch functions.
 
-Run in a container where the reference project is present (its path is the
-REFERENCE_DIR environment variable, default /root/reference):
+Run where the reference project is present, with its checkout directory in the
+REFERENCE_DIR environment variable:
 
-    python tests/golden/make_golden.py
+    REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 
 The reference's exhaustive_benchmark_suite.py imports its CUDA extension at
 top level; a stub module is installed under that name first, and only the
@@ -34,7 +34,9 @@ SUBSAMPLE = 4096
 
 
 def load_reference():
-    ref_dir = os.environ.get("REFERENCE_DIR", "/root/reference")
+    ref_dir = os.environ.get("REFERENCE_DIR")
+    if not ref_dir:
+        raise SystemExit("set REFERENCE_DIR to the reference project's checkout directory")
     sys.modules.setdefault("mla_custom_cuda", types.ModuleType("mla_custom_cuda"))
     sys.path.insert(0, ref_dir)
     import exhaustive_benchmark_suite as ebs  # noqa: E402
