@@ -423,9 +423,9 @@ def main_ours(args):
             "stages": stages,
             "roofline": {"bound": "hbm", "kernel": "mla_attention (cache read)",
                          "achieved": att_gbs, "peak": hbm, "unit": "GB/s", "frac": att_gbs / hbm,
-                         "traffic": (1.566e9 if (args.config == "c1" and precision == "tensor" and shard == "batch") else None),
-                         "traffic_source": "ncu capture of mla_decode_tc_kernel at c1 "
-                                           "(profiles/mla_decode_tc_kernel_c1.md)",
+                         "traffic": (1.565e9 if (args.config == "c1" and precision == "tensor" and shard == "batch") else None),
+                         "traffic_source": "ncu capture of mla_decode_tc_kernel at c1: dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum per launch (1.530 GB + 0.035 GB)",
                          "peak_source": peak_src,
                          "algorithmic_bytes_per_launch": cache_b,
                          "note": "mla_attention stage = fused tcgen05 decode kernel + segment combine + W_uv "
