@@ -42,7 +42,7 @@ METRIC = "MLA decode layer-forward tokens/s at B=128,Sk=4989 (us/layer and cache
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=1500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=sorted(mc.CONFIGS))
     ap.add_argument("--precision", default="tensor", choices=["exact", "tensor"])
@@ -56,6 +56,9 @@ def parse():
                     help="multi-GPU layout: batch (weak scaling, default) or keys (strong scaling, default for c2)")
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the timed layer forwards one by one instead of replaying a CUDA graph of one")
+    ap.add_argument("--no-parity", action="store_true", help="skip the sampled-sequence parity check")
+    ap.add_argument("--no-key-shard-c2", action="store_true",
+                    help="with --gpus N > 1, skip the extra key-sharded c2 measurement")
     ap.add_argument("--qprep", default="redundant", choices=["heads", "redundant"],
                     help="key sharding: Q-prep repeated on every rank (default), or sharded by heads + all-gather of q")
     return ap.parse_args()
@@ -76,9 +79,28 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def workload_bytes(w: mc.Workload, B: int):
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def line_config(w: mc.Workload, world: int, shard: str) -> dict:
+    """The workload keys both arms (ours and the reference) print identically."""
+    return {**w.describe(), "global_batch": w.batch * (world if shard == "batch" else 1),
+            "parallelism": f"batch-shard dp{world}" if shard == "batch" else f"key-shard sp{world}",
+            "l2": "no flush: inputs larger than L2 (c_kv + pe_cache %.2f GB per GPU)"
+                  % (workload_bytes(w, w.batch)[0] / world ** (shard == "keys") / 1e9)}
+
+
+def workload_bytes(w: mc.Workload, B: int, sk=None):
     es = torch.tensor([], dtype=w.dtype).element_size()
-    cache = B * w.sk * (w.kv_rank + w.rope) * es
+    cache = B * (w.sk if sk is None else sk) * (w.kv_rank + w.rope) * es
     weights = (w.hidden * w.q_lora + w.q_lora + w.q_lora * w.heads * (w.nope + w.rope)
                + 2 * w.heads * w.kv_rank * w.nope) * es
     acts = B * w.sq * (w.hidden + w.heads * w.v_dim) * es
@@ -145,6 +167,13 @@ class ClockSampler:
 
 KEY_SHARDED = {"on": False, "heads": False}
 
+# DRAM bytes per launch of the decode kernel, from the ncu capture named below
+# (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (config, precision,
+# shard, world).
+TRAFFIC = {("c1", "tensor", "batch", 1): 1.565e9}
+TRAFFIC_SOURCE = ("profiles/mla_decode_tc_kernel_c1.md: ncu capture of mla_decode_tc_kernel at c1, "
+                  "dram__bytes_read.sum + dram__bytes_write.sum of one launch")
+
 
 def run_forward(mcc, t, w, precision):
     if KEY_SHARDED["heads"]:
@@ -187,7 +216,7 @@ def cpu_baseline(w: mc.Workload, reps: int = 3):
             best = min(best, time.perf_counter() - t0)
     tokens = w.batch * w.sq
     return {"value": tokens / best, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "ms_per_step": best * 1e3,
+            "cpu_model": cpu_model(), "ms_per_step": best * 1e3,
             "sample": f"full {w.name} forward ({w.batch} sequences), fp32, oracle/mla_oracle.py "
                       f"(the reference's torch ops), best of {reps}"}
 
@@ -215,12 +244,102 @@ def main_reference(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,1) cache / activations, N(0,0.02) weights)",
-            "config": {**w.describe(), "note": "reference PyTorch path on host CPU cores"},
+            "config": line_config(w, 1, "batch"),
+            "note": "reference PyTorch path (restated in oracle/mla_oracle.py) on host CPU cores",
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "cpu_model": cpu_model(),
                              "sample": f"full {w.name} forward per step, oracle/mla_oracle.py (the reference's "
                                        f"torch ops), {threads} threads"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def device_timed(stream, fn, n, warm=3):
+    """Average device time (ms) of fn() over n calls, CUDA events on `stream`."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def max_over_ranks(v: float, world: int, dev) -> float:
+    if world == 1:
+        return v
+    tt = torch.tensor([v], device=dev)
+    torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+    return float(tt.item())
+
+
+def parity_sample(mcc, t, w, precision, seqs):
+    """rel-L2 of the GPU layer output against the fp64 oracle, and the
+    argmax-of-scores agreement, on a few sequences of the benched inputs."""
+    from oracle import mla_oracle as orc
+    qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                               w.nope, w.rope, mc.EPS, precision=precision)
+    out = mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, causal=w.causal,
+                               precision=precision)
+    torch.cuda.synchronize()
+    W = {k: t[k].double().cpu() for k in ("W_q_a", "q_norm_w", "W_q_b", "W_uk", "W_uv")}
+    errs, agree = [], []
+    for b in seqs:
+        x = t["x"][b:b + 1].double().cpu()
+        ck, pe = t["c_kv"][b:b + 1].cpu(), t["pe_cache"][b:b + 1].cpu()
+        rqa, rqr = orc.q_absorbed(x, W["W_q_a"], W["q_norm_w"], W["W_q_b"], W["W_uk"], t["positions"].cpu())
+        ref = orc.mla_attention(rqa, rqr, ck.double(), pe.double(), W["W_uv"], w.scale, w.causal)
+        o = out[b:b + 1].double().cpu()
+        errs.append(float((o - ref).norm() / ref.norm()))
+        gq, gr = qa[b:b + 1].cpu(), qr[b:b + 1].cpu()
+        gk, gp = ck, pe
+        if precision == "tensor":   # the operands the tensor-core kernel multiplies
+            gq, gr, gk, gp = (v.to(torch.bfloat16) for v in (gq, gr, gk, gp))
+        s = orc.scores(gq.double(), gr.double(), gk.double(), gp.double(), w.scale, w.causal)
+        r = orc.scores(rqa, rqr, ck.double(), pe.double(), w.scale, w.causal)
+        agree.append(float((s.argmax(-1) == r.argmax(-1)).double().mean()))
+    return {"sequences": list(seqs), "rel_l2_vs_fp64_oracle": errs, "max_rel_l2": max(errs),
+            "tolerance": 1e-5 if precision == "exact" else 2e-2,
+            "argmax_agreement": agree, "min_argmax_agreement": min(agree)}
+
+
+def key_shard_c2(mcc, dev, rank, world, steps, precision):
+    """Config c2 (B=4, Sk=65536) key-sharded over all ranks inside this run:
+    every rank holds 1/world of every sequence's keys, the partials are
+    all-gathered over NCCL and merged (strong scaling of one decode step)."""
+    from mla_custom_cuda import sharding
+    w = mc.CONFIGS["c2"]
+    k0, k1 = sharding.key_shard(w.sk, rank, world)
+    t = mc.make_inputs(w, device=dev, gen="device", seed=1234)
+    t["c_kv"] = t["c_kv"][:, k0:k1].contiguous()
+    t["pe_cache"] = t["pe_cache"][:, k0:k1].contiguous()
+    stream = torch.cuda.current_stream(dev)
+
+    def q():
+        return mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                                 w.nope, w.rope, mc.EPS, precision=precision)
+
+    def step():
+        qa, qr = q()
+        return sharding.sk_sharded_attention(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
+                                             precision=precision)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    ms = max_over_ranks(device_timed(stream, step, steps, warm=0), world, dev)
+    q_ms = max_over_ranks(device_timed(stream, q, steps), world, dev)
+    qa, qr = q()
+    att_ms = max_over_ranks(device_timed(stream, lambda: mcc.mla_attention_partial(
+        qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, precision=precision), steps), world, dev)
+    return {"workload": w.name, "ranks": world, "tokens_per_s": w.batch * w.sq / (ms * 1e-3), "ms_per_step": ms,
+            "q_absorbed_ms_per_rank": q_ms, "partial_attention_ms_per_rank": att_ms,
+            "all_gather_and_merge_ms": max(ms - q_ms - att_ms, 0.0), "keys_per_rank": k1 - k0,
+            "timing": "CUDA events on each rank, max over ranks"}
 
 
 def main_ours(args):
@@ -239,11 +358,13 @@ def main_ours(args):
     shard = args.shard or ("keys" if args.config == "c2" else "batch")
     if world == 1:
         shard = "batch"
+    sk_local = w.sk
     if shard == "keys":
         if w.causal:
             raise SystemExit("key sharding is for non-causal decode")
         from mla_custom_cuda import sharding
         k0, k1 = sharding.key_shard(w.sk, rank, world)
+        sk_local = k1 - k0
         t = mc.make_inputs(w, device=dev, gen="device", seed=1234)   # same queries / weights on every rank
         t["c_kv"] = t["c_kv"][:, k0:k1].contiguous()
         t["pe_cache"] = t["pe_cache"][:, k0:k1].contiguous()
@@ -259,23 +380,11 @@ def main_ours(args):
         if world > 1:
             torch.distributed.barrier()
 
-    def timed(fn, n):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n):
-            fn()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / n
-
     # ---- device-resident timed region (whole layer forward, headline precision).
     # The clock sampler starts before the warm-up, which runs for at least W steps
     # and at least --min-warmup-s seconds so nvidia-smi samples a loaded GPU.
     # Batch-sharded steps hold no collective: one layer forward (q_absorbed_ex +
-    # mla_attention_ex, 9 kernels) is captured once in a CUDA graph and replayed
+    # mla_attention_ex, 8 kernels) is captured once in a CUDA graph and replayed
     # per step, which removes the host launch gaps; the kernels and their work are
     # the same as an eager call's.
     use_graph = not args.no_graph and not KEY_SHARDED["on"]
@@ -325,48 +434,63 @@ def main_ours(args):
         torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-        ms = float(tt.item())
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world, dev)
     tokens_total = B * w.sq * (world if shard == "batch" else 1)
     value = tokens_total / (ms * 1e-3)
+    dev_status = mcc.device_status(dev)   # a kernel that gave up on a bounded wait invalidates the run
+    if dev_status:
+        raise SystemExit(f"device-side failure code {dev_status} during the timed region")
 
-    # ---- per-stage timing (same stream, CUDA events; inputs larger than L2)
-    n_att = max(5, args.steps)
+    # ---- per-stage timing (same stream, CUDA events; inputs larger than L2), and
+    # the decode-attention kernel alone (event pair around each of its launches)
+    n_att = max(5, min(args.steps, 200))
     stages = {}
+    kernel_ms = None
     for prec in ((precision,) if args.no_stages else ("tensor", "exact")):
         if KEY_SHARDED["heads"]:
             # local stages of a rank: Q-prep of its heads, attention over its key shard
             from mla_custom_cuda import sharding
             qa, qr = sharding.head_sharded_q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
                                                       t["positions"], w.nope, w.rope, mc.EPS, precision=prec)
-            att = timed(lambda: mcc.mla_attention_partial(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
-                                                          precision=prec), n_att)
         else:
             qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
                                        w.nope, w.rope, mc.EPS, precision=prec)
-            att = timed(lambda: mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
-                                                     causal=w.causal, precision=prec), n_att)
-        qp = timed(lambda: mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
-                                             t["positions"], w.nope, w.rope, mc.EPS, precision=prec), n_att)
+        if KEY_SHARDED["on"]:
+            att_fn = lambda: mcc.mla_attention_partial(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,  # noqa
+                                                       precision=prec)
+        else:
+            att_fn = lambda: mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,  # noqa
+                                                  causal=w.causal, precision=prec)
+        if prec == "tensor":
+            mcc.kernel_timing(True)
+        att = device_timed(stream, att_fn, n_att)
+        if prec == "tensor":
+            tot, cnt = mcc.kernel_timing()
+            mcc.kernel_timing(False)
+            kernel_ms = max_over_ranks(tot / max(cnt, 1), world, dev) if cnt else None
+        att = max_over_ranks(att, world, dev)
+        qp = max_over_ranks(device_timed(stream, lambda: mcc.q_absorbed_ex(
+            t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"], w.nope, w.rope, mc.EPS,
+            precision=prec), n_att), world, dev)
         fwd = att + qp if prec != precision else ms
         stages[prec] = {"q_absorbed_ms": qp, "mla_attention_ms": att, "layer_ms": fwd,
-                        "tokens_per_s": B * w.sq / (fwd * 1e-3)}
+                        "tokens_per_s": tokens_total / (fwd * 1e-3)}
+        if prec == "tensor" and kernel_ms:
+            stages[prec]["decode_kernel_ms"] = kernel_ms
     att_ms = stages[precision]["mla_attention_ms"]
     q_ms = stages[precision]["q_absorbed_ms"]
 
-    cache_b, weight_b, act_b = workload_bytes(w, B)
+    cache_b, weight_b, act_b = workload_bytes(w, B, sk_local)
     qf, af = workload_flops(w, B)
     hbm, bf16_tf, peak_src = peaks()
-    att_gbs = cache_b / (att_ms * 1e-3) / 1e9
+    # the dominant kernel (decode attention) when it ran, else the attention stage
+    dom_ms = kernel_ms if (precision == "tensor" and kernel_ms) else att_ms
+    dom_gbs = cache_b / (dom_ms * 1e-3) / 1e9
 
     # ---- end to end through the public API: the step's hidden states come from
     # pinned host memory and the layer output goes back to pinned host memory;
     # the KV cache and weights stay resident in HBM, as in a decode server.
-    e2e = None
-    if not args.no_e2e:
+    def e2e_run(prec):
         x_host = t["x"].cpu().pin_memory()
         pos_host = t["positions"].cpu().pin_memory()
         out_host = torch.empty((B, w.sq, w.heads, w.v_dim), dtype=w.dtype).pin_memory()
@@ -375,28 +499,32 @@ def main_ours(args):
         def e2e_step():
             t2["x"] = x_host.to(dev, non_blocking=True)
             t2["positions"] = pos_host.to(dev, non_blocking=True)
-            o, _, _ = run_forward(mcc, t2, w, precision)
+            o, _, _ = run_forward(mcc, t2, w, prec)
             out_host.copy_(o, non_blocking=True)
 
         for _ in range(3):
             e2e_step()
         torch.cuda.synchronize()
         barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        e_ms = e0.elapsed_time(e1) / args.steps
-        if world > 1:
-            tt = torch.tensor([e_ms], device=dev)
-            torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-            e_ms = float(tt.item())
-        e2e = {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
-               "h2d_bytes_per_step": x_host.numel() * x_host.element_size() + pos_host.numel() * 8,
-               "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
-               "resident": "KV cache (c_kv, pe_cache) and weights stay in HBM"}
+        e_ms = max_over_ranks(device_timed(stream, e2e_step, args.steps if prec == precision else n_att, warm=0),
+                              world, dev)
+        return {"value": tokens_total / (e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e_ms,
+                "h2d_bytes_per_step": x_host.numel() * x_host.element_size() + pos_host.numel() * 8,
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+                "resident": "KV cache (c_kv, pe_cache) and weights stay in HBM"}
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_run(precision)
+        if not args.no_stages:
+            for prec in stages:
+                if prec != precision:
+                    stages[prec]["e2e"] = e2e_run(prec)
+
+    # ---- c2 key-sharded across all ranks (strong scaling), when several GPUs run
+    key_c2 = None
+    if world > 1 and shard == "batch" and not args.no_key_shard_c2:
+        key_c2 = key_shard_c2(mcc, dev, rank, world, max(20, min(args.steps, 200)), precision)
 
     # our kernels per layer forward (fp32 storage): tensor = 2a1 GEMM, RMSNorm, 2a2 GEMM,
     # RoPE/gather, 2c GEMM, decode attention, segment combine, W_uv GEMM; exact = the
@@ -406,6 +534,9 @@ def main_ours(args):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_baseline(w)
+        parity = None
+        if not args.no_parity and not KEY_SHARDED["on"]:
+            parity = parity_sample(mcc, t, w, precision, sorted({0, B - 1}))
         dtype_name = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16"}[w.dtype]
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -415,27 +546,37 @@ def main_ours(args):
                      ("bf16" if w.dtype != torch.float16 else "f16") + " tensor-core operands, f32 accumulate, "
                      + dtype_name + " storage",
             "data": "synthetic (seeded N(0,1) cache / activations, N(0,0.02) weights)",
-            "config": {**w.describe(), "global_batch": B * (world if shard == "batch" else 1), "precision": precision,
-                       "launch": ("CUDA graph of one layer forward (q_absorbed_ex + mla_attention_ex), replayed per step"
-                                  if use_graph else "eager calls per step"),
-                       "parallelism": f"batch-shard dp{world}" if shard == "batch" else (f"key-shard sp{world} (NCCL all-gather + LSE merge)" + (", Q-prep head-sharded + all-gather of q" if KEY_SHARDED["heads"] else "")),
-                       "l2": "inputs larger than L2 (cache %.2f GB per GPU)" % (cache_b / 1e9)},
+            "config": line_config(w, world, shard),
+            "precision": precision,
+            "launch": ("CUDA graph of one layer forward (q_absorbed_ex + mla_attention_ex), replayed per step"
+                       if use_graph else "eager calls per step")
+                      + (", Q-prep head-sharded + all-gather of q" if KEY_SHARDED["heads"] else ""),
             "stages": stages,
-            "roofline": {"bound": "hbm", "kernel": "mla_attention (cache read)",
-                         "achieved": att_gbs, "peak": hbm, "unit": "GB/s", "frac": att_gbs / hbm,
-                         "traffic": (1.565e9 if (args.config == "c1" and precision == "tensor" and shard == "batch") else None),
-                         "traffic_source": "ncu capture of mla_decode_tc_kernel at c1: dram__bytes_read.sum + "
-                                           "dram__bytes_write.sum per launch (1.530 GB + 0.035 GB)",
-                         "peak_source": peak_src,
+            "roofline": {"bound": "hbm",
+                         "kernel": ("mla_decode_tc_kernel (tensor-core decode attention)"
+                                    if dom_ms is kernel_ms else "mla_attention stage"),
+                         "achieved": dom_gbs, "peak": hbm, "unit": "GB/s", "frac": dom_gbs / hbm,
+                         "kernel_ms": dom_ms,
+                         "traffic": TRAFFIC.get((args.config, precision, shard, world)),
+                         "traffic_source": TRAFFIC_SOURCE,
+                         "peak_source": peak_src + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
                          "algorithmic_bytes_per_launch": cache_b,
-                         "note": "mla_attention stage = fused tcgen05 decode kernel + segment combine + W_uv "
-                                 "projection; algorithmic bytes = c_kv + pe_cache read once"},
+                         "algorithmic_bytes": "c_kv + pe_cache of this rank read once: B x Sk_local x 576 x "
+                                              "element size",
+                         "stage_frac": cache_b / (att_ms * 1e-3) / 1e9 / hbm,
+                         "note": "achieved = algorithmic bytes / the decode kernel's average CUDA-event time "
+                                 "(event pair around each launch on its stream); stage_frac uses the whole "
+                                 "mla_attention stage (decode kernel + segment combine + W_uv projection)"},
             "tflops": {"q_absorbed": qf / (q_ms * 1e-3) / 1e12, "mla_attention": af / (att_ms * 1e-3) / 1e12},
             "clocks": clk.summary(),
             "gpu_launches": launches_per_step * args.steps,
+            "device_status": dev_status,
+            "parity": parity,
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
+        if key_c2 is not None:
+            line["key_shard_c2"] = key_c2
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

@@ -46,7 +46,8 @@ typedef enum mla_status {
     MLA_ERR_INVALID_ARGUMENT = 1, /* bad shape, null pointer or inconsistent sizes   */
     MLA_ERR_UNSUPPORTED = 2,      /* dtype / precision / shape combination not built */
     MLA_ERR_WORKSPACE = 3,        /* workspace pointer null or smaller than required */
-    MLA_ERR_CUDA = 4              /* a CUDA runtime call or kernel launch failed     */
+    MLA_ERR_CUDA = 4,             /* a CUDA runtime call or kernel launch failed     */
+    MLA_ERR_DEVICE = 5            /* a kernel gave up on a bounded wait (see below)  */
 } mla_status_t;
 
 /* Storage dtype of every floating-point operand and output of one call. The
@@ -202,6 +203,41 @@ MLA_API mla_status_t mla_attention_noalloc(
     int64_t kv_rank, int64_t rope, int64_t v_dim,
     double scale, int causal,
     void* out, void* stream);
+
+/* ------------------------------------------------------ device failure status --
+ * No counterpart in the reference, whose kernels can only hang or succeed
+ * (its host reports launch and shared-memory opt-in failures,
+ * mla_kernels.cu:141-146). Every mbarrier wait of this library's tensor-core
+ * kernels is bounded by wall time (2 s by default). A wait that runs out
+ * records a non-zero code in a per-device status block (the first code
+ * wins), and the kernel drains its in-flight copies and MMAs, frees its TMEM
+ * and returns; the outputs of that call are invalid. The code stays set until
+ * cleared.
+ *
+ * mla_device_status: waits for `stream`, reads the code of the current
+ *   device into *code, and returns MLA_ERR_DEVICE if it is non-zero.
+ * mla_device_status_clear: enqueues a reset of the code on `stream`.
+ * mla_set_wait_limit_ns: sets the wait bound of later launches on the
+ *   current device (0 restores the default); synchronises `stream`.
+ * mla_wait_selftest: launches a kernel whose one bounded wait is on a barrier
+ *   that nothing completes, so it runs out after the wait limit and records
+ *   code 900. Used by tests to check the reporting path.
+ */
+MLA_API mla_status_t mla_device_status(void* stream, int* code);
+MLA_API mla_status_t mla_device_status_clear(void* stream);
+MLA_API mla_status_t mla_set_wait_limit_ns(uint64_t ns, void* stream);
+MLA_API mla_status_t mla_wait_selftest(void* stream);
+
+/* ------------------------------------------------------------ kernel timing --
+ * Benchmark hook (no counterpart in the reference, which times stages with
+ * CUDA events from Python, stage_profile.py:31-41). While enabled, every launch
+ * of the tensor-core decode-attention kernel is bracketed by a CUDA event pair
+ * on its stream (at most 8192 launches are kept). mla_timing_read waits for
+ * the recorded launches, returns their summed device time and count, and
+ * starts a new count. Do not enable it during CUDA graph capture.
+ */
+MLA_API mla_status_t mla_timing_enable(int on);
+MLA_API mla_status_t mla_timing_read(double* total_ms, int64_t* launches);
 
 /* Size in bytes of the fixed scratch array used by mla_attention_noalloc. */
 MLA_API size_t mla_attention_noalloc_max_scratch(void);

@@ -116,6 +116,7 @@ const char* mla_status_string(mla_status_t s) {
         case MLA_ERR_UNSUPPORTED: return "unsupported";
         case MLA_ERR_WORKSPACE: return "workspace too small";
         case MLA_ERR_CUDA: return "CUDA error";
+        case MLA_ERR_DEVICE: return "device-side failure";
     }
     return "unknown status";
 }

@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(256) ctx_reduce_kernel(
 struct T3Plan {
     int64_t rows_b, rows_total, ld, chunk, ntiles;
     int slices;
-    size_t off_err, off_S, off_tmax, off_max, off_sum, off_parts, off_ctx, total;
+    size_t off_S, off_tmax, off_max, off_sum, off_parts, off_ctx, total;
 };
 
 T3Plan make_t3plan(const AArgs& a) {
@@ -478,7 +478,6 @@ T3Plan make_t3plan(const AArgs& a) {
     p.chunk = cb * 32;
     p.slices = int(ceil_div(kblocks, cb));
     size_t off = 0;
-    p.off_err = off;   off = align_up(off + 256, 256);
     p.off_S = off;     off = align_up(off + size_t(p.rows_total) * p.ld * sizeof(float), 256);
     p.ntiles = ceil_div(p.ld, 128);
     p.off_tmax = off;  off = align_up(off + size_t(p.rows_total) * p.ntiles * sizeof(float), 256);
@@ -499,14 +498,14 @@ bool t3_supported(const AArgs& a) {
 mla_status_t attn_exact_t3(const AArgs& a, cudaStream_t st) {
     const T3Plan p = make_t3plan(a);
     char* ws = static_cast<char*>(a.workspace);
-    int* err = reinterpret_cast<int*>(ws + p.off_err);
+    DeviceStatus* dst = nullptr;
+    MLA_TRY(device_status_block(&dst));
+    int* err = &dst->code;
     float* S = reinterpret_cast<float*>(ws + p.off_S);
     float* rmax = reinterpret_cast<float*>(ws + p.off_max);
     float* rsum = reinterpret_cast<float*>(ws + p.off_sum);
     float* parts = reinterpret_cast<float*>(ws + p.off_parts);
     float* ctx = reinterpret_cast<float*>(ws + p.off_ctx);
-    if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
-        return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
 
     // S[b] = q_absorbed[b] [rows_b, R] @ c_kv[b]^T + q_rope[b] @ pe[b]^T in one GEMM (the
     // rope pair is a second K phase); keys past sk read as zeros (TMA fill) and land

@@ -36,6 +36,23 @@ template <> __device__ __forceinline__ double neg_inf<double>() { return -__long
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Per-device failure status of the kernels (status.cu). `code` is the first
+// bounded-wait timeout code recorded (0 = none); `wait_limit_ns` bounds every
+// mbarrier wait. Kernels get a pointer to `code`; the limit sits 8 bytes after it.
+struct DeviceStatus {
+    int code;
+    int reserved;
+    unsigned long long wait_limit_ns;
+};
+constexpr int kErrSelftestTimeout = 900;
+
+// Device address of this device's status block (looked up once per device).
+mla_status_t device_status_block(DeviceStatus** out);
+
+// Benchmark hook: an event pair around the decode-attention kernel when
+// mla_timing_enable(1) is in effect (status.cu).
+void timing_mark(cudaStream_t st, bool begin);
+
 // Records a message for mla_last_error_message() and returns the status.
 mla_status_t set_error(mla_status_t st, const char* fmt, ...);
 

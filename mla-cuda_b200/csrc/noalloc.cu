@@ -63,7 +63,7 @@ MLA_API mla_status_t mla_attention_noalloc(
     if (batch * sq > 0 && sk > 0 && !mla::tc_attention_supported(a))
         return mla::set_error(MLA_ERR_UNSUPPORTED,
                               "MLA no-alloc attention: shape not covered by the tensor-core kernel "
-                              "(needs heads=128, kv_rank=512, rope=64)");
+                              "(needs heads=128, kv_rank=512, rope=64 and batch*sk < 2^31)");
     size_t need = 0;
     MLA_TRY(mla_attention_workspace_size(dtype, MLA_PREC_TENSOR, batch, sq, sk, heads, kv_rank, rope, v_dim, causal,
                                          &need));

@@ -509,7 +509,7 @@ namespace {
 struct QTPlan {
     int split1, split2;
     int64_t chunk1, chunk2;
-    size_t off_err, off_p1, off_qlat, off_p2, off_qnope, off_cs, total;
+    size_t off_p1, off_qlat, off_p2, off_qnope, off_cs, total;
 };
 
 // Split-K plan of a weight-streaming GEMM (one CTA per SM): the slice count s
@@ -545,7 +545,6 @@ QTPlan make_tplan(const QArgs& a) {
     p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), M, a.hidden, bk, p.chunk1);
     p.split2 = tc_split(mt * ceil_div(ncols, 128), M, a.q_lora, bk, p.chunk2);
     size_t off = 0;
-    p.off_err = off;   off = align_up(off + 256, 256);
     p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(Acc), 256);
     p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(T), 256);
     p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(Acc), 256);
@@ -581,14 +580,13 @@ mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3) {
     const int64_t M = a.batch * a.sq;
     const int64_t ncols = a.heads * (a.nope + a.rope);
     char* ws = static_cast<char*>(a.workspace);
-    int* err = reinterpret_cast<int*>(ws + p.off_err);
+    DeviceStatus* dst = nullptr;
+    MLA_TRY(device_status_block(&dst));
+    int* err = &dst->code;
     Acc* P1 = reinterpret_cast<Acc*>(ws + p.off_p1);
     T* q_lat = reinterpret_cast<T*>(ws + p.off_qlat);
     Acc* P2 = reinterpret_cast<Acc*>(ws + p.off_p2);
     T* q_nope_t = reinterpret_cast<T*>(ws + p.off_qnope);
-    if (cudaMemsetAsync(err, 0, sizeof(int), st) != cudaSuccess)
-        return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
-
     TcGemm g1{};   // 2a1: x [M, hidden] @ W_q_a [hidden, q_lora]
     g1.A = a.x; g1.a_dims[0] = a.hidden; g1.a_dims[1] = 1; g1.a_dims[2] = M; g1.a_ld[0] = a.hidden; g1.a_ld[1] = a.hidden;
     g1.B = a.W_q_a; g1.b_mn = true; g1.b_dims[0] = a.q_lora; g1.b_dims[1] = a.hidden; g1.b_dims[2] = 1;

@@ -15,7 +15,7 @@
 namespace mla {
 namespace sm100 {
 
-constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s per wait
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // default: 2 s per wait
 // try_wait suspends the waiting thread in hardware for up to this long (it
 // resumes as soon as the phase completes), instead of spinning on issue slots
 // that the warps sharing its SM sub-partition need.
@@ -72,15 +72,18 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 }
 
 // Bounded wait. `abort` is a shared flag raised by any thread that timed out;
-// `err` is the kernel's global error word (the first failure code wins).
+// `err` is the `code` word of the device's status block (DeviceStatus in
+// common.cuh: the first failure code wins; the wait limit in ns follows 8 bytes
+// after it).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
                                           int code, bool cluster_scope = false) {
     if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
+    const uint64_t limit = *reinterpret_cast<const volatile unsigned long long*>(err + 2);
     while (true) {
         if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > limit) {
             *abort = 1;
             atomicCAS(err, 0, code);
             return false;

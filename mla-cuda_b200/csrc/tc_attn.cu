@@ -784,7 +784,7 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint
 struct Plan {
     int64_t groups, total_tiles, tiles_per_cluster, nclusters;
     int max_segs;
-    size_t off_err, off_O, off_ml, off_norm, total;
+    size_t off_O, off_ml, off_norm, total;
 };
 
 int64_t tiles_of(const AArgs& a, int64_t q) {
@@ -814,7 +814,6 @@ Plan make_plan(const AArgs& a) {
     pl.max_segs = int((pl.tiles_per_cluster + min_tiles - 1) / min_tiles + 1);
     const int64_t slots = pl.nclusters * pl.max_segs;
     size_t off = 0;
-    pl.off_err = off;  off = align_up(off + 256, 256);
     pl.off_O = off;    off = align_up(off + size_t(slots) * kHeads * kRank * 4, 256);
     pl.off_ml = off;   off = align_up(off + size_t(slots) * kHeads * 2 * 4, 256);
     pl.off_norm = off; off = align_up(off + size_t(pl.groups) * kHeads * kRank * 4, 256);
@@ -848,7 +847,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         p.qr = a.q_rope;
         p.O_part = reinterpret_cast<float*>(ws + pl.off_O);
         p.ml = reinterpret_cast<float*>(ws + pl.off_ml);
-        p.err = reinterpret_cast<int*>(ws + pl.off_err);
+        DeviceStatus* dst = nullptr;
+        MLA_TRY(device_status_block(&dst));
+        p.err = &dst->code;
         p.batch = a.batch; p.sq = a.sq; p.sk = a.sk; p.causal = a.causal;
         p.c_log2 = float(1.4426950408889634 / a.scale);
         p.total_tiles = pl.total_tiles;
@@ -864,8 +865,6 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, 64, box_rows, swz))
             return set_error(MLA_ERR_CUDA, "MLA: cuTensorMapEncodeTiled failed (alignment of c_kv / pe_cache?)");
 
-        if (cudaMemsetAsync(p.err, 0, sizeof(int), st) != cudaSuccess)
-            return set_error(MLA_ERR_CUDA, "MLA: memset of the error word failed");
         auto kern = mla_decode_tc_kernel<T>;
         const size_t smem = smem_bytes<T>();
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
@@ -882,14 +881,16 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         int* trace_host = nullptr;
+        const size_t trace_bytes = size_t(2 * pl.nclusters) * 32 * sizeof(int);   // 32 words per CTA
         if (getenv("MLA_TC_TRACE")) {   // debug: progress words polled from the host while the kernel runs
-            if (cudaHostAlloc(reinterpret_cast<void**>(&trace_host), 2 * 148 * 32 * sizeof(int), cudaHostAllocMapped) ==
-                cudaSuccess) {
-                memset(trace_host, 0xff, 2 * 148 * 32 * sizeof(int));
+            if (cudaHostAlloc(reinterpret_cast<void**>(&trace_host), trace_bytes, cudaHostAllocMapped) == cudaSuccess) {
+                memset(trace_host, 0xff, trace_bytes);
                 cudaHostGetDevicePointer(reinterpret_cast<void**>(&p.trace), trace_host, 0);
             }
         }
+        timing_mark(st, true);
         const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p);
+        timing_mark(st, false);
         if (le != cudaSuccess) {
             cudaGetLastError();
             return set_error(MLA_ERR_CUDA, "MLA: launch of the tensor-core attention kernel failed: %s",
@@ -904,7 +905,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             const bool done = cudaEventQuery(ev) == cudaSuccess;
             fprintf(stderr, "[mla trace] kernel %s; grid %lld CTAs\n", done ? "finished" : "STILL RUNNING after 5 s",
                     (long long)(2 * pl.nclusters));
-            for (int64_t b = 0; b < 2 * pl.nclusters && b < 296; ++b) {
+            for (int64_t b = 0; b < 2 * pl.nclusters; ++b) {
                 const volatile int* t = trace_host + b * 32;
                 fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d | kcyc total %d "
                         "stg_empty %d bf_empty(p) %d p_full %d q_ready %d bf_full %d s_full %d x_full %d o_resc %d "
@@ -912,6 +913,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                         (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[23], t[8], t[9], t[10], t[11], t[12],
                         t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25], t[26], t[27], t[28], t[29], t[30], t[31]);
             }
+            // a kernel still running may write the buffer: keep it mapped (leaked) in that case
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);
         }

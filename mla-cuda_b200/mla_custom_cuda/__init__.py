@@ -38,6 +38,8 @@ __all__ = [
     "q_absorbed", "mla_attention", "q_absorbed_ex", "mla_attention_ex",
     "mla_attention_partial", "lse_combine",
     "set_precision", "get_precision", "library_path", "abi_version",
+    "device_status", "clear_device_status", "check_device", "set_wait_limit_ns", "wait_selftest",
+    "kernel_timing",
 ]
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmla_b200.so"
@@ -77,10 +79,25 @@ def _load() -> ctypes.CDLL:
                                           + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
     lib.mla_lse_combine.restype = ctypes.c_int
     lib.mla_lse_combine.argtypes = [ctypes.c_int] + [_c_i64] * 3 + [_c_vp] * 5
+    lib.mla_device_status.restype = ctypes.c_int
+    lib.mla_device_status.argtypes = [_c_vp, ctypes.POINTER(ctypes.c_int)]
+    lib.mla_device_status_clear.restype = ctypes.c_int
+    lib.mla_device_status_clear.argtypes = [_c_vp]
+    lib.mla_set_wait_limit_ns.restype = ctypes.c_int
+    lib.mla_set_wait_limit_ns.argtypes = [ctypes.c_uint64, _c_vp]
+    lib.mla_wait_selftest.restype = ctypes.c_int
+    lib.mla_wait_selftest.argtypes = [_c_vp]
+    lib.mla_timing_enable.restype = ctypes.c_int
+    lib.mla_timing_enable.argtypes = [ctypes.c_int]
+    lib.mla_timing_read.restype = ctypes.c_int
+    lib.mla_timing_read.argtypes = [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_int64)]
     return lib
 
 
 _lib = _load()
+# MLA_CHECK=1: after every call, wait for the stream and raise RuntimeError if a
+# kernel recorded a device-side failure (costs a synchronisation per call).
+_checked = os.environ.get("MLA_CHECK", "0").strip() not in ("", "0")
 _precision = os.environ.get("MLA_PRECISION", "exact").strip().lower()
 if _precision not in _PRECISIONS:
     raise ImportError(f"mla_custom_cuda: MLA_PRECISION must be one of {sorted(_PRECISIONS)}")
@@ -106,6 +123,73 @@ def set_precision(precision: str) -> None:
 
 def get_precision() -> str:
     return _precision
+
+
+def _stream_of(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_status(device=None) -> int:
+    """Waits for the current stream of `device` and returns the device-side
+    failure code of the library's kernels there (0 = none). A non-zero code
+    means a kernel gave up on a bounded wait; the outputs of that call are
+    invalid. The code stays set until clear_device_status()."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    code = ctypes.c_int(0)
+    with torch.cuda.device(device):
+        st = _lib.mla_device_status(_stream_of(device), ctypes.byref(code))
+    if st not in (0, 5):   # 5 = MLA_ERR_DEVICE: reported through the code
+        _raise_status(st, "device_status")
+    return int(code.value)
+
+
+def check_device(device=None) -> None:
+    """Raises RuntimeError if a kernel recorded a device-side failure on `device`."""
+    code = device_status(device)
+    if code:
+        raise RuntimeError(f"mla_custom_cuda: device-side failure code {code}: "
+                           f"{_lib.mla_last_error_message().decode(errors='replace')}")
+
+
+def clear_device_status(device=None) -> None:
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_device_status_clear(_stream_of(device)), "clear_device_status")
+
+
+def set_wait_limit_ns(ns: int, device=None) -> None:
+    """Bound on every mbarrier wait of later kernel launches on `device` (0 restores
+    the default of 2 s)."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_set_wait_limit_ns(int(ns), _stream_of(device)), "set_wait_limit_ns")
+
+
+def wait_selftest(device=None) -> None:
+    """Launches a kernel whose single bounded wait is on a barrier nothing
+    completes; after the wait limit it records code 900 in the device status."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_wait_selftest(_stream_of(device)), "wait_selftest")
+
+
+def kernel_timing(enable: Optional[bool] = None):
+    """Device time of the tensor-core decode-attention kernel alone.
+
+    kernel_timing(True) starts recording an event pair around each of its
+    launches; kernel_timing() returns (total_ms, launches) since the last read;
+    kernel_timing(False) stops. Not for use inside CUDA graph capture."""
+    if enable is not None:
+        _raise_status(_lib.mla_timing_enable(int(bool(enable))), "kernel_timing")
+        return None
+    ms, n = ctypes.c_double(0.0), ctypes.c_int64(0)
+    _raise_status(_lib.mla_timing_read(ctypes.byref(ms), ctypes.byref(n)), "kernel_timing")
+    return float(ms.value), int(n.value)
+
+
+def _after_call(device) -> None:
+    if _checked:
+        check_device(device)
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -181,6 +265,7 @@ def q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim: int, rop
                                  rope_dim, R, float(eps), qa.data_ptr(), qr.data_ptr(), ws.data_ptr(),
                                  ws.numel(), stream)
     _raise_status(st, "q_absorbed")
+    _after_call(device)
     return [qa, qr]
 
 
@@ -228,6 +313,7 @@ def mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float, cau
                                 wv.data_ptr(), B, Sq, Sk, H, R, D, V, float(scale), int(bool(causal)),
                                 out.data_ptr(), ws.data_ptr(), ws.numel(), stream)
     _raise_status(st, "mla_attention")
+    _after_call(device)
     return out
 
 
@@ -271,6 +357,7 @@ def mla_attention_partial(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float
                                         lse.data_ptr(), ws.data_ptr(), ws.numel(),
                                         torch.cuda.current_stream(device).cuda_stream)
     _raise_status(st, "mla_attention_partial")
+    _after_call(device)
     return out, lse
 
 

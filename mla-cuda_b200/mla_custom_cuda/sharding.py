@@ -113,7 +113,14 @@ def gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None) -> Tuple[t
 def sk_sharded_attention(q_absorbed, q_rope, c_kv_local, pe_local, W_uv, scale: float, group=None,
                          precision: Optional[str] = None) -> torch.Tensor:
     """Attention over keys sharded across the ranks of `group`: every rank passes
-    the same queries and its own key shard; every rank gets the full output."""
+    the same queries and its own key shard; every rank gets the full output.
+
+    fp64 is rejected before any work: the shards' log-sum-exp travel in fp32,
+    which would cap an fp64 merge at fp32 accuracy (mla_lse_combine has no fp64
+    variant for that reason)."""
+    if q_absorbed.dtype == torch.float64:
+        raise RuntimeError("sk_sharded_attention: fp64 is not supported (the merge weights are fp32); "
+                           "run fp64 attention unsharded")
     import mla_custom_cuda as mcc
     out, lse = mcc.mla_attention_partial(q_absorbed, q_rope, c_kv_local, pe_local, W_uv, scale,
                                          precision=precision)

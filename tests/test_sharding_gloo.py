@@ -154,3 +154,85 @@ def test_gather_partials_keeps_rank_order_and_dtypes():
         assert p.exitcode == 0
     res = sorted(q.get() for _ in range(world))
     assert all(ok for _, ok in res), res
+
+
+def test_key_sharded_attention_rejects_fp64_before_any_work():
+    """fp64 would lose its accuracy in the fp32 merge weights: rejected before the
+    partial attention or the collective runs (no process group is needed)."""
+    from mla_custom_cuda import sharding
+    qa = torch.zeros(1, 1, 128, 512, dtype=torch.float64)
+    with pytest.raises(RuntimeError, match="fp64"):
+        sharding.sk_sharded_attention(qa, qa[..., :64], qa[0], qa[0, ..., :64], qa[0], 1.0)
+
+
+def _failing_rank_worker(rank, world, port, result_q):
+    """Rank 1 leaves between steps (exits after step 0); rank 0 must learn it from
+    its next collective, which ends with an error within the process group's
+    short timeout instead of hanging."""
+    import datetime
+    import sys
+    for p in (str(ROOT), str(PKG)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from mla_custom_cuda import sharding
+    out = torch.randn(1, 1, 2, 8, dtype=torch.float32)
+    lse = torch.randn(1, 1, 2)
+    sharding.gather_partials(out, lse)            # step 0: both ranks
+    if rank == 1:
+        result_q.put((rank, "left"))
+        result_q.close()
+        result_q.join_thread()
+        os._exit(0)                                # leaves without tearing down the group
+    try:
+        sharding.gather_partials(out, lse)        # step 1: the peer is gone
+        result_q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - any error from the collective is the signal
+        result_q.put((rank, f"error: {type(e).__name__}"))
+    result_q.close()
+    result_q.join_thread()
+    os._exit(0)
+
+
+def test_rank_that_leaves_is_detected_by_the_next_collective():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+        assert p.exitcode == 0
+    res = dict(q.get() for _ in range(world))
+    assert res[1] == "left"
+    assert res[0].startswith("error"), res
+
+
+def _init_failure_worker(port, result_q):
+    """A rank whose peer never joins: init_process_group must fail with an error
+    after its timeout (the host-side form of a failed communicator set-up)."""
+    import datetime
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=0, world_size=2, timeout=datetime.timedelta(seconds=3))
+        result_q.put("joined")
+    except Exception as e:  # noqa: BLE001
+        result_q.put(f"error: {type(e).__name__}")
+    result_q.close()
+    result_q.join_thread()
+    os._exit(0)
+
+
+def test_process_group_init_failure_is_reported():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_init_failure_worker, args=(_free_port(), q))
+    p.start()
+    p.join(90)
+    assert p.exitcode == 0
+    assert q.get(timeout=5).startswith("error")
