@@ -6,25 +6,26 @@
 // up-projection (3d, mla_kernels.cu:1339-1476). Scores never reach memory.
 //
 // Work unit. A "group" is one (b, q): the 128 heads of query q of sequence b,
-// which share the keys of sequence b. Each group is cut into 32-key tiles; all
+// which share the keys of sequence b. Each group is cut into 64-key tiles; all
 // tiles of all groups are laid end to end and split evenly over the persistent
 // clusters (stream-K), so every SM gets the same number of key tiles whatever
 // B and Sk are. A cluster's tiles of one group form a "segment"; each segment
 // leaves an unnormalised partial output plus its (max, sum) for the combine.
 //
-// Cluster of two CTAs (one per SM). The 512 latent dims are split between
-// them: CTA r owns c_kv dims [256r, 256r+256) and CTA 1 also the 64 rope dims.
-// Per key tile each CTA
+// Cluster of two CTAs (one per SM). The 576 score dims are split evenly
+// between them: CTA r owns c_kv dims [256r, 256r+256) and rope dims
+// [32r, 32r+32). Per key tile each CTA
 //   * loads only its own dims of the tile (TMA), once from HBM;
 //   * computes a partial score S_r = Q[:, dims_r] . K[:, dims_r]^T on the
-//     tensor cores (M = 128 heads, N = 32 keys, K = 256 or 320) into TMEM;
+//     tensor cores (M = 128 heads, N = 64 keys, K = 288) into TMEM;
 //   * swaps S_r with its peer through distributed shared memory, so both
 //     hold S = S_0 + S_1 bit-identically and run the same online softmax;
 //   * accumulates its half of the context, O_r += P . V[:, 256r:256r+256]
-//     (M = 128, N = 256, K = 32) in TMEM. The same shared-memory tile is the
+//     (M = 128, N = 256, K = 64) in TMEM. The same shared-memory tile is the
 //     K-major B operand of the score MMA and the MN-major B operand of P.V.
-// TMEM per CTA: O half 256 columns, three score/probability buffers of 32, the
-// bf16 query slice 128 or 160 (A operand read from TMEM) - 512 columns in all.
+// TMEM per CTA (512 columns): O half 256, two score / probability buffers of
+// 64, the bf16 latent query slice 128 (A operand read from TMEM). The 32 rope
+// dims of the query are an A operand in shared memory.
 //
 // Operands are bf16 (fp16 for fp16 storage) with fp32 accumulation. fp32
 // storage is converted to bf16 in shared memory after the TMA load, so HBM
@@ -58,61 +59,63 @@ namespace tc {
 
 using namespace sm100;
 
-constexpr int NK = 32;                    // keys per tile
+constexpr int NK = 64;                      // keys per tile
 constexpr int kHeads = 128;
 constexpr int kRank = 512;
 constexpr int kRope = 64;
-constexpr int kHalf = 256;                // latent dims per CTA
+constexpr int kHalf = 256;                  // latent dims per CTA
+constexpr int kRopeHalf = 32;               // rope dims per CTA
 constexpr int kThreads = 256;
-constexpr int kConvThreads = 64;         // fp32 -> bf16 converter threads (warps 2, 3)
-constexpr int kChunkBytes = NK * 128;     // one 64-dim chunk of a tile (128-byte rows)
-constexpr int kSlotBytes = 5 * kChunkBytes;
-constexpr int kStgRows = NK / 2;          // an fp32 staging buffer holds half a key tile
-constexpr int kStgBytes = kStgRows * (kHalf + kRope) * 4;
-constexpr int kXBufs = 4;                 // partial-score exchange buffers (see the softmax role)
-constexpr int kXBytes = kHeads * NK * 4;  // one buffer: 128 rows x 32 fp32, 16-byte chunks XOR-swizzled by row
+constexpr int kConvThreads = 64;            // fp32 -> bf16 converter threads (warps 2, 3)
+constexpr int kChunkBytes = NK * 128;       // 64 latent dims of a tile: 64 rows of 128 B, 128B swizzle
+constexpr int kRopeChunkBytes = NK * 64;    // 32 rope dims of a tile: 64 rows of 64 B, 64B swizzle
+constexpr int kSlotBytes = 4 * kChunkBytes + kRopeChunkBytes;
+constexpr int kStgRows = 16;                // an fp32 staging buffer holds a quarter of a key tile
+constexpr int kStgLatBytes = kStgRows * kHalf * 4;
+constexpr int kStgBytes = kStgRows * (kHalf + kRopeHalf) * 4;
+constexpr int kXBufs = 2;                   // partial-score exchange buffers (flow-controlled)
+constexpr int kXBytes = kHeads * NK * 4;    // one buffer: 128 rows x 64 fp32, 16-byte chunks XOR-swizzled by row
+constexpr int kQRopeBytes = kHeads * kRopeHalf * 2;   // rope query slice: 128 rows of 64 B, 64B swizzle
 
 // TMEM columns: O half, kSBufs score / probability buffers, the query slice.
 constexpr uint32_t kTmemO = 0;
-constexpr int kSBufs = 3;
+constexpr int kSBufs = 2;
 constexpr uint32_t kTmemS = 256;
-constexpr uint32_t kTmemQ = 256 + kSBufs * NK;   // up to 160 columns, ends at column 512
+constexpr uint32_t kTmemQ = 256 + kSBufs * NK;   // 128 columns, ends at column 512
 constexpr uint32_t kTmemCols = 512;
+static_assert(kTmemQ + kHalf / 2 == kTmemCols, "TMEM budget");
 
 enum : int { ERR_TIMEOUT_BASE = 100 };
 
-#ifndef MLA_TC_F32_SLOTS
-#define MLA_TC_F32_SLOTS 6
-#endif
-#ifndef MLA_TC_F32_STAGES
-#define MLA_TC_F32_STAGES 2
-#endif
 template <typename T> struct Traits;
 template <> struct Traits<float> {
     static constexpr bool kConvert = true;
-    static constexpr int kSlots = MLA_TC_F32_SLOTS;
-    static constexpr int kStages = MLA_TC_F32_STAGES;
+    static constexpr int kSlots = 3;
+    static constexpr int kStages = 2;
     static constexpr uint32_t kFmt = 1;     // bf16 operands
 };
 template <> struct Traits<__nv_bfloat16> {
-    static constexpr bool kConvert = false; static constexpr int kSlots = 6; static constexpr int kStages = 0;
+    static constexpr bool kConvert = false; static constexpr int kSlots = 4; static constexpr int kStages = 0;
     static constexpr uint32_t kFmt = 1;
 };
 template <> struct Traits<__half> {
-    static constexpr bool kConvert = false; static constexpr int kSlots = 6; static constexpr int kStages = 0;
+    static constexpr bool kConvert = false; static constexpr int kSlots = 4; static constexpr int kStages = 0;
     static constexpr uint32_t kFmt = 0;     // fp16 operands
 };
 
-// Shared memory: kSlots 128B-swizzled 16-bit key tiles (the MMA operands),
-// kStages fp32 half-tile staging buffers (fp32 storage only), kXBufs exchange
-// buffers, barriers. 16-bit storage is loaded by TMA straight into the slots;
-// fp32 storage lands in staging, which the converter warps release as soon as
-// they have read it (so TMA keeps loads in flight), and is converted into slots.
+// Shared memory: kSlots 16-bit key tiles (the MMA operands: four 128B-swizzled
+// latent chunks and one 64B-swizzled rope chunk each), kStages fp32
+// quarter-tile staging buffers (fp32 storage only), the exchange buffers, the
+// rope query slice, barriers. 16-bit storage is loaded by TMA straight into
+// the slots; fp32 storage lands in staging, which the converter warps release
+// as soon as they have read it (so TMA keeps loads in flight), and is
+// converted into slots.
 template <typename T>
 constexpr size_t smem_bytes() {
     return 1024 /*align slack*/ + size_t(Traits<T>::kSlots) * kSlotBytes + size_t(Traits<T>::kStages) * kStgBytes +
-           kXBufs * size_t(kXBytes) + 1024 /*barriers*/;
+           kXBufs * size_t(kXBytes) + kQRopeBytes + 1024 /*barriers*/;
 }
+static_assert(smem_bytes<float>() <= 232448 && smem_bytes<__nv_bfloat16>() <= 232448, "shared memory budget");
 
 struct Params {
     const void* qa;     // [B*Sq*H, 512]
@@ -141,17 +144,6 @@ __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
 __device__ __forceinline__ void trace_put(const Params& p, int role, int64_t v) {
     if (p.trace) *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 32 + role) = int(v);
 }
-
-// Debug wait accounting: cycles spent per wait site, compiled in only with
-// -DMLA_TC_PROFILE (build with MLA_TC_PROFILE=1) and reported by MLA_TC_TRACE.
-#ifdef MLA_TC_PROFILE
-#define MLA_TW(slot, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); \
-    wacc[slot] += clock64() - _t0; return _r; }())
-#define MLA_PROF(stmt) stmt
-#else
-#define MLA_TW(slot, expr) (expr)
-#define MLA_PROF(stmt)
-#endif
 
 struct TileIter {
     int64_t g, j, tiles, keys;
@@ -194,34 +186,20 @@ struct Bars {
     uint64_t s_full[kSBufs];
     uint64_t p_full[kSBufs];
     uint64_t o_done[kSBufs];
-    uint64_t x_full[kXBufs];  // peer's partial scores arrived (st.async byte count)
+    uint64_t x_full[kXBufs][4];   // per softmax warp: peer's partial scores arrived (st.async byte count)
+    uint64_t x_free[kXBufs][4];   // per softmax warp: the peer has read my push into its buffer
     uint64_t q_ready;
     uint32_t tmem_base;
     int abort;
 };
+static_assert(sizeof(Bars) <= 1024, "barrier area");
 
-// P.V of tile i: O += P(i) . V(i) (M = 128 heads, N = 256 latent dims, K = 32 keys),
-// A = P from TMEM, B = the key tile's latent half, MN-major, 128B swizzle (LBO =
-// stride between 64-dim chunks, SBO = stride between 8-key groups). Releases the
-// slot and signals o_done. Out of line: the MMA thread issues it from three places.
-template <int kSlots>
-__device__ __noinline__ bool issue_pv_mma(Bars* bars, uint32_t tmem, uint32_t smem_slots, int64_t i, bool first,
-                                          volatile int* abort, int* err, uint32_t idesc_o) {
-    const int sb = int(i % kSBufs);
-    if (!mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, err, ERR_TIMEOUT_BASE + 3)) return false;
-    tc_fence_after();
-    const int sl = int(i % kSlots);
-    const uint32_t base = smem_slots + sl * kSlotBytes;
-    const uint32_t p_tmem = tmem + kTmemS + sb * NK;
-    const uint64_t vd0 = smem_desc(base, kChunkBytes, 1024, 2);
-#pragma unroll
-    for (int k = 0; k < NK / 16; ++k)
-        mma_ts(tmem + kTmemO, p_tmem + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4), idesc_o,
-               (first && k == 0) ? 0u : 1u);
-    mma_commit(&bars->bf_empty[sl]);
-    mma_commit(&bars->o_done[sb]);
-    return true;
-}
+// 64B-swizzled byte offset of 16-byte unit u (0..3) of row r in a region of
+// 64-byte rows (the layout TMA's SWIZZLE_64B writes and the MMA descriptor's
+// 64-byte swizzle mode reads).
+__device__ __forceinline__ uint32_t swz64(uint32_t r, uint32_t u) { return r * 64u + ((u ^ ((r >> 1) & 3u)) << 4); }
+// 128B-swizzled byte offset of 16-byte unit u (0..7) of row r (128-byte rows).
+__device__ __forceinline__ uint32_t swz128(uint32_t r, uint32_t u) { return r * 128u + ((u ^ (r & 7u)) << 4); }
 
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
@@ -233,19 +211,17 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     unsigned char* slots = smem;
     unsigned char* stg = slots + Tr::kSlots * kSlotBytes;
     float* xbuf = reinterpret_cast<float*>(stg + Tr::kStages * kStgBytes);
-    Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<unsigned char*>(xbuf) + kXBufs * kXBytes);
+    unsigned char* qrope = reinterpret_cast<unsigned char*>(xbuf) + kXBufs * kXBytes;
+    Bars* bars = reinterpret_cast<Bars*>(qrope + kQRopeBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
     const uint32_t peer = rank ^ 1u;
-    const int dims = rank == 0 ? kHalf : kHalf + kRope;   // score dims of this CTA
     const int64_t cl = cluster_id_x();
     const int64_t t_begin = cl * p.tiles_per_cluster;
     const int64_t t_end = min(t_begin + p.tiles_per_cluster, p.total_tiles);
     const int64_t n = t_end > t_begin ? t_end - t_begin : 0;   // tiles of this cluster
     volatile int* abort = &bars->abort;
-    MLA_PROF(long long wacc[20] = {0};)
-    MLA_PROF(const long long t_kernel0 = clock64();)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 6; ++i) {
@@ -259,7 +235,11 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             mbar_init(&bars->p_full[i], 128);
             mbar_init(&bars->o_done[i], 1);
         }
-        for (int i = 0; i < kXBufs; ++i) mbar_init(&bars->x_full[i], 1);
+        for (int i = 0; i < kXBufs; ++i)
+            for (int w = 0; w < 4; ++w) {
+                mbar_init(&bars->x_full[i][w], 1);
+                mbar_init(&bars->x_free[i][w], 1);
+            }
         mbar_init(&bars->q_ready, 128);
         bars->abort = 0;
         fence_mbar_init();
@@ -279,151 +259,151 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
         if (warp == 0 && lane == 0) {
             // ------------------------------------------------------------ TMA producer
             TileIter it = locate(p, t_begin);
-            const uint32_t bytes = uint32_t(NK) * dims * sizeof(T);
             for (int64_t i = 0; i < n; ++i, advance(p, it)) {
                 const int32_t row = int32_t((it.g / p.sq) * p.sk + it.j * NK);
                 trace_put(p, 0, i * 16 + 1);
                 if constexpr (Tr::kConvert) {
                     bool okp = true;
-                    for (int h = 0; h < 2 && okp; ++h) {
-                        const int64_t k = 2 * i + h;
+                    for (int h = 0; h < NK / kStgRows && okp; ++h) {
+                        const int64_t k = int64_t(NK / kStgRows) * i + h;
                         const int st = int(k % Tr::kStages);
-                        okp = MLA_TW(0, mbar_wait(&bars->stg_empty[st], uint32_t(((k / Tr::kStages) & 1) ^ 1), abort,
-                                                  p.err, ERR_TIMEOUT_BASE + 1));
+                        okp = mbar_wait(&bars->stg_empty[st], uint32_t(((k / Tr::kStages) & 1) ^ 1), abort, p.err,
+                                        ERR_TIMEOUT_BASE + 1);
                         if (!okp) break;
                         unsigned char* dst = stg + st * kStgBytes;
-                        mbar_arrive_expect_tx(&bars->full[st], bytes / 2);
+                        mbar_arrive_expect_tx(&bars->full[st], uint32_t(kStgBytes));
                         tma_load_2d(dst, &tm_ckv, &bars->full[st], int32_t(rank * kHalf), row + h * kStgRows);
-                        if (rank == 1)
-                            tma_load_2d(dst + kStgRows * kHalf * 4, &tm_pe, &bars->full[st], 0, row + h * kStgRows);
+                        tma_load_2d(dst + kStgLatBytes, &tm_pe, &bars->full[st], int32_t(rank * kRopeHalf),
+                                    row + h * kStgRows);
                     }
                     if (!okp) break;
                 } else {
                     const int sl = int(i % Tr::kSlots);
-                    if (!MLA_TW(1, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                                             ERR_TIMEOUT_BASE + 2)))
+                    if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 2))
                         break;
                     unsigned char* dst = slots + sl * kSlotBytes;
-                    mbar_arrive_expect_tx(&bars->full[sl], bytes);
+                    mbar_arrive_expect_tx(&bars->full[sl], uint32_t(kSlotBytes));
                     for (int c = 0; c < 4; ++c)
                         tma_load_2d(dst + c * kChunkBytes, &tm_ckv, &bars->full[sl], int32_t(rank * kHalf + c * 64), row);
-                    if (rank == 1) tma_load_2d(dst + 4 * kChunkBytes, &tm_pe, &bars->full[sl], 0, row);
+                    tma_load_2d(dst + 4 * kChunkBytes, &tm_pe, &bars->full[sl], int32_t(rank * kRopeHalf), row);
                 }
             }
         } else if (warp == 1) {
             // ------------------------------------------------------------ MMA issuer
-            // Order: S(j) then P.V of tile j-2. P.V trails by two tiles (also across
-            // segment boundaries), so the score MMA of the tile the softmax is
-            // preparing never queues behind a P.V on the tensor pipe.
+            // Order per tile i: the score MMA S(i), then P.V of tile i-1. S(i) writes
+            // score buffer i%2, whose previous contents P(i-2) were consumed by
+            // P.V(i-2), issued one iteration earlier (tcgen05 MMAs of one thread run
+            // in issue order).
             if (lane == 0) {
                 constexpr uint32_t idesc_s = instr_desc(Tr::kFmt, 128, NK, 0, 0);
                 constexpr uint32_t idesc_o = instr_desc(Tr::kFmt, 128, kHalf, 0, 1);
                 const uint32_t smem_slots = smem_u32(slots);
+                const uint64_t qd0 = smem_desc(smem_u32(qrope), 16, 512, 4);
                 TileIter it = locate(p, t_begin);
                 int64_t seg = 0;
                 bool ok = true;
-                bool first_ring[kSBufs] = {true, true, true};
+                bool prev_first = false;
+                // P.V of tile i: O += P(i) . V(i) (M = 128 heads, N = 256 latent dims,
+                // K = 64 keys), A = P from TMEM, B = the key tile's latent half,
+                // MN-major, 128B swizzle (LBO = stride between 64-dim chunks, SBO =
+                // stride between 8-key groups). Releases the slot, signals o_done.
                 auto issue_pv = [&](int64_t i, bool first) -> bool {
-                    return issue_pv_mma<Tr::kSlots>(bars, tmem, smem_slots, i, first, abort, p.err, idesc_o);
+                    const int sb = int(i % kSBufs);
+                    if (!mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3))
+                        return false;
+                    tc_fence_after();
+                    const int sl = int(i % Tr::kSlots);
+                    const uint32_t base = smem_slots + sl * kSlotBytes;
+                    const uint32_t p_tmem = tmem + kTmemS + sb * NK;
+                    const uint64_t vd0 = smem_desc(base, kChunkBytes, 1024, 2);
+#pragma unroll
+                    for (int k = 0; k < NK / 16; ++k)
+                        mma_ts(tmem + kTmemO, p_tmem + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4), idesc_o,
+                               (first && k == 0) ? 0u : 1u);
+                    mma_commit(&bars->bf_empty[sl]);
+                    mma_commit(&bars->o_done[sb]);
+                    return true;
                 };
-                int64_t pv_done = 0;   // P.V issued for tiles [0, pv_done)
                 for (int64_t i = 0; i < n && ok; ++i) {
                     const bool first = (i == 0) || it.j == 0;
                     if (first) {
-                        // Before waiting for this segment's query, issue the pending P.V up
-                        // to tile i-2: the softmax may be waiting for one of them (the
-                        // epilogue of a one-tile segment i-2, a rescale) before it loads
-                        // the query. P.V of tile i-1 stays behind: its softmax follows the
-                        // query load.
-                        for (; ok && pv_done < i - 1; ++pv_done) ok = issue_pv(pv_done, first_ring[pv_done % kSBufs]);
-                        if (!ok) break;
-                        if (!MLA_TW(3, mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)))
-                            break;
+                        if (!mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)) break;
                         ++seg;
                     }
                     const int sl = int(i % Tr::kSlots);
                     trace_put(p, 1, i * 16 + 1);
                     uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
-                    if (!MLA_TW(4, mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)))
-                        break;
+                    if (!mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)) break;
                     tc_fence_after();
                     const uint32_t base = smem_slots + sl * kSlotBytes;
                     const int sb = int(i % kSBufs);
-                    MLA_PROF(const long long tsi = clock64();)
-                    // B = K [32 keys x 16 dims], K-major, 128B swizzle: chunk k/4, +32 B per
-                    // k-step. One descriptor per tile; each k-step adds a compile-time offset
-                    // to its start-address field (16-byte units), so the issuing thread does
-                    // one add per MMA.
+                    // B = K [64 keys x 16 dims], K-major: latent chunk k/4 (128B swizzle,
+                    // +32 B per k-step), then the rope chunk (64B swizzle, +32 B per
+                    // k-step) against the rope query slice in shared memory.
                     const uint64_t bd0 = smem_desc(base, 16, 1024, 2);
+                    const uint64_t rd0 = smem_desc(base + 4 * kChunkBytes, 16, 512, 4);
                     const uint32_t d_s = tmem + kTmemS + sb * NK;
 #pragma unroll
                     for (int k = 0; k < kHalf / 16; ++k)
                         mma_ts(d_s, tmem + kTmemQ + k * 8,
                                bd0 + uint64_t(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4), idesc_s, k > 0 ? 1u : 0u);
-                    if (rank == 1) {
 #pragma unroll
-                        for (int k = kHalf / 16; k < (kHalf + kRope) / 16; ++k)
-                            mma_ts(d_s, tmem + kTmemQ + k * 8,
-                                   bd0 + uint64_t(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4), idesc_s, 1u);
-                    }
+                    for (int k = 0; k < kRopeHalf / 16; ++k)
+                        mma_ss(d_s, qd0 + uint64_t((k * 32) >> 4), rd0 + uint64_t((k * 32) >> 4), idesc_s, 1u);
                     mma_commit(&bars->s_full[sb]);
-                    MLA_PROF(wacc[17] += clock64() - tsi;)
                     trace_put(p, 1, i * 16 + 2);
-                    first_ring[i % kSBufs] = first;
-                    if (i >= 2 && pv_done == i - 2) {   // P.V trails the score MMA by two tiles
-                        ok = issue_pv(i - 2, first_ring[(i - 2) % kSBufs]);
-                        pv_done = i - 1;
-                    }
+                    if (i >= 1) ok = issue_pv(i - 1, prev_first);
+                    prev_first = first;
                     advance(p, it);
                 }
-                for (; ok && pv_done < n; ++pv_done) ok = issue_pv(pv_done, first_ring[pv_done % kSBufs]);
+                if (ok && n > 0) issue_pv(n - 1, prev_first);
             }
         } else if (warp >= 4 && warp < 8) {
             // ------------------------------------------------------------ softmax
             // Pipelined one tile ahead: iteration i first "prepares" tile i+1 (loads
             // the next segment's query if one starts, waits for its partial scores,
-            // pushes them to the peer) and then finishes tile i (adds the peer's
-            // partial, online softmax, P to TMEM, epilogue), so the DSMEM round trip
-            // of tile i+1 overlaps the softmax of tile i.
-            // Exchange buffers: the peer can be at most three pushes ahead of my
-            // reads (its push of tile k+1 follows its softmax of k-1, which needed my
-            // push of k-1, made after my softmax of k-3), so four buffers need no
-            // further flow control.
+            // pushes them to the peer) and then finishes tile i (reloads its own
+            // partial from TMEM, adds the peer's, online softmax, P to TMEM,
+            // epilogue), so the DSMEM round trip of tile i+1 overlaps the softmax
+            // of tile i. Exchange buffer b (= tile % 2) of this warp's 32 rows is
+            // pushed into by the peer's matching warp only after this warp has told
+            // it (x_free) that it read the buffer's previous tile.
             const int row = threadIdx.x - 128;               // head
-            const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+            const int wq = warp & 3;
+            const uint32_t lane_off = uint32_t(wq * 32) << 16;
             const float c = p.c_log2;
             const float tau = 8.0f / c;                      // lazy rescale threshold (raw units)
             const uint32_t sw = uint32_t(row & 7);            // chunk swizzle of my exchange row
-            // peer addresses of my exchange row and of the exchange barriers (buffer 0;
-            // the mapping is linear: buffer b is at +b*kXBytes / +b*8)
+            // peer addresses of my exchange row and of my warp's exchange barriers
+            // (buffer 0; buffer b is at +b*kXBytes / +b*4*8 bytes)
             const uint32_t xpeer0 = map_peer(xbuf + row * NK, peer);
-            const uint32_t xbar_peer0 = map_peer(&bars->x_full[0], peer);
+            const uint32_t xbar_peer0 = map_peer(&bars->x_full[0][wq], peer);
             int64_t seg_local = 0;
             float m_run = -INFINITY, l_run = 0.f;
             bool ok = true;
 
-            // prepare tile i (iterator itp): my partial scores of tile i are returned in sr
-            auto prepare = [&](int64_t i, const TileIter& itp, uint32_t (&sr)[32]) __attribute__((always_inline)) -> bool {
+            auto prepare = [&](int64_t i, const TileIter& itp) __attribute__((always_inline)) -> bool {
                 const bool first = (i == 0) || itp.j == 0;
                 const int sb = int(i % kSBufs);
                 if (first) {
-                    // query slice of this group into TMEM as bf16/fp16 pairs: 16-byte
-                    // loads, 64 dims (32 TMEM columns) per chunk, all loads of a chunk
-                    // issued before any conversion
+                    // query of this group: the latent slice into TMEM as bf16/fp16
+                    // pairs (32 dims = 16 TMEM columns per step, all 16-byte loads
+                    // of a step issued before any conversion), the rope slice into
+                    // shared memory (64B-swizzled K-major A operand)
                     __syncwarp();   // tcgen05.st below is warp-collective
                     const int64_t grow = itp.g * kHeads + row;
                     const T* qa = static_cast<const T*>(p.qa) + grow * kRank + rank * kHalf;
-                    const T* qr = static_cast<const T*>(p.qr) + grow * kRope;
+                    const T* qr = static_cast<const T*>(p.qr) + grow * kRope + rank * kRopeHalf;
                     constexpr int kV = 16 / sizeof(T);           // elements per 16-byte vector
-                    const int nchunks = rank == 1 ? 5 : 4;
-                    for (int c32 = 0; c32 < nchunks; ++c32) {
-                        const T* srcp = c32 < 4 ? qa + c32 * 64 : qr;
-                        uint4 v[64 / kV];
+                    for (int c16 = 0; c16 < kHalf / 32; ++c16) {
+                        uint4 v[32 / kV];
 #pragma unroll
-                        for (int q = 0; q < 64 / kV; ++q) v[q] = __ldg(reinterpret_cast<const uint4*>(srcp) + q);
-                        uint32_t r[32];
+                        for (int q = 0; q < 32 / kV; ++q)
+                            v[q] = __ldg(reinterpret_cast<const uint4*>(qa + c16 * 32) + q);
+                        uint32_t r[16];
 #pragma unroll
-                        for (int q = 0; q < 64 / kV; ++q) {
+                        for (int q = 0; q < 32 / kV; ++q) {
                             if constexpr (sizeof(T) == 4) {
                                 r[2 * q] = pack_bf16(__uint_as_float(v[q].x), __uint_as_float(v[q].y));
                                 r[2 * q + 1] = pack_bf16(__uint_as_float(v[q].z), __uint_as_float(v[q].w));
@@ -431,67 +411,104 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                                 r[4 * q] = v[q].x; r[4 * q + 1] = v[q].y; r[4 * q + 2] = v[q].z; r[4 * q + 3] = v[q].w;
                             }
                         }
-                        tmem_st32(tmem + lane_off + kTmemQ + c32 * 32, r);
+                        tmem_st16(tmem + lane_off + kTmemQ + c16 * 16, r);
+                    }
+                    {
+                        uint4 v[kRopeHalf / kV];
+#pragma unroll
+                        for (int q = 0; q < kRopeHalf / kV; ++q) v[q] = __ldg(reinterpret_cast<const uint4*>(qr) + q);
+                        uint32_t r[16];
+#pragma unroll
+                        for (int q = 0; q < kRopeHalf / kV; ++q) {
+                            if constexpr (sizeof(T) == 4) {
+                                r[2 * q] = pack_bf16(__uint_as_float(v[q].x), __uint_as_float(v[q].y));
+                                r[2 * q + 1] = pack_bf16(__uint_as_float(v[q].z), __uint_as_float(v[q].w));
+                            } else {
+                                r[4 * q] = v[q].x; r[4 * q + 1] = v[q].y; r[4 * q + 2] = v[q].z; r[4 * q + 3] = v[q].w;
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            *reinterpret_cast<uint4*>(qrope + swz64(uint32_t(row), uint32_t(u))) =
+                                make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2], r[4 * u + 3]);
                     }
                     tmem_st_wait();
+                    fence_proxy_async_smem();   // the rope slice is read by the tensor cores (async proxy)
                     tc_fence_before();
                     mbar_arrive(&bars->q_ready);
                 }
                 if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 1);
                 // every lane polls, then the warp reconverges: tcgen05.ld is warp-collective
-                if (!__all_sync(0xffffffffu, MLA_TW(5, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort,
-                                                                 p.err, ERR_TIMEOUT_BASE + 6))))
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
+                                                       ERR_TIMEOUT_BASE + 6)))
                     return false;
                 tc_fence_after();
-                MLA_PROF(const long long tph = clock64();)
-                tmem_ld32(tmem + lane_off + kTmemS + sb * NK, sr);
-                tmem_ld_wait();
                 const int xb = int(i % kXBufs);
-                // one thread announces the bytes the peer will push for tile i; then
-                // st.async pushes my partial, counted on the peer's barrier
-                if (row == 0) mbar_arrive_expect_tx(&bars->x_full[xb], uint32_t(kHeads * NK * 4));
-                for (int e = 0; e < NK / 4; ++e)
-                    st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + ((uint32_t(e) ^ sw) << 4), __uint_as_float(sr[4 * e]),
-                                __uint_as_float(sr[4 * e + 1]), __uint_as_float(sr[4 * e + 2]),
-                                __uint_as_float(sr[4 * e + 3]), xbar_peer0 + uint32_t(xb) * 8u);
-                MLA_PROF(wacc[11] += clock64() - tph;)
+                const int64_t k = i / kXBufs;
+                // the peer's buffer xb must no longer hold tile i-2 unread
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_free[xb][wq], uint32_t((k & 1) ^ 1), abort, p.err,
+                                                       ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true)))
+                    return false;
+                // lane 0 announces the bytes the peer will push into my buffer for tile
+                // i; then st.async pushes my partial, counted on the peer's barrier
+                if (lane == 0) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 4));
+#pragma unroll
+                for (int h = 0; h < NK / 32; ++h) {   // 32 keys at a time
+                    uint32_t sr[32];
+                    tmem_ld32(tmem + lane_off + kTmemS + sb * NK + h * 32, sr);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + ((uint32_t(h * 8 + e) ^ sw) << 4),
+                                    __uint_as_float(sr[4 * e]), __uint_as_float(sr[4 * e + 1]),
+                                    __uint_as_float(sr[4 * e + 2]), __uint_as_float(sr[4 * e + 3]),
+                                    xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
+                }
                 if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 3);
                 return true;
             };
 
             TileIter it = locate(p, t_begin);     // tile being finished
             TileIter itn = it;                     // tile being prepared
-            uint32_t sr_cur[32], sr_next[32];
-            MLA_PROF(const long long t_loop0 = clock64();)
-            ok = prepare(0, itn, sr_cur);
+            ok = prepare(0, itn);
             for (int64_t i = 0; i < n && ok; ++i) {
                 const bool first = (i == 0) || it.j == 0;
                 const bool last = (i + 1 == n) || (it.j + 1 == it.tiles);
                 const int sb = int(i % kSBufs);
                 if (i + 1 < n) {
                     advance(p, itn);
-                    if (!prepare(i + 1, itn, sr_next)) break;
+                    if (!prepare(i + 1, itn)) break;
                 }
                 if (first) {
                     m_run = -INFINITY;
                     l_run = 0.f;
                 }
                 const int xb = int(i % kXBufs);
-                if (!__all_sync(0xffffffffu, MLA_TW(6, mbar_wait(&bars->x_full[xb], uint32_t((i / kXBufs) & 1), abort,
-                                                                 p.err, ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true))))
+                if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_full[xb][wq], uint32_t((i / kXBufs) & 1), abort, p.err,
+                                                       ERR_TIMEOUT_BASE + 8, /*cluster_scope=*/true)))
                     break;
-                MLA_PROF(const long long tph = clock64();)
+                // my partial of tile i, reloaded from TMEM (the buffer is not reused
+                // before P.V(i) is issued), plus the peer's partial
                 float s[NK];
-                const int64_t key0 = it.j * NK;
+                {
+                    uint32_t* su = reinterpret_cast<uint32_t*>(s);
+                    tmem_ld32(tmem + lane_off + kTmemS + sb * NK, *reinterpret_cast<uint32_t(*)[32]>(&su[0]));
+                    tmem_ld32(tmem + lane_off + kTmemS + sb * NK + 32, *reinterpret_cast<uint32_t(*)[32]>(&su[32]));
+                }
                 const float* xr = xbuf + xb * (kHeads * NK) + row * NK;
+                tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < NK / 4; ++e) {
                     const float4 pv = *reinterpret_cast<const float4*>(xr + ((e ^ int(sw)) << 2));
-                    s[4 * e] = __uint_as_float(sr_cur[4 * e]) + pv.x;
-                    s[4 * e + 1] = __uint_as_float(sr_cur[4 * e + 1]) + pv.y;
-                    s[4 * e + 2] = __uint_as_float(sr_cur[4 * e + 2]) + pv.z;
-                    s[4 * e + 3] = __uint_as_float(sr_cur[4 * e + 3]) + pv.w;
+                    s[4 * e] += pv.x;
+                    s[4 * e + 1] += pv.y;
+                    s[4 * e + 2] += pv.z;
+                    s[4 * e + 3] += pv.w;
                 }
+                // my reads of the exchange buffer are done: the peer may push tile i+2
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(&bars->x_free[xb][wq], peer);
+                const int64_t key0 = it.j * NK;
                 if (key0 + NK > it.keys) {            // ragged last tile of a group (warp-uniform)
                     const int valid = int(it.keys - key0);
 #pragma unroll
@@ -509,12 +526,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     // new maximum (alpha <= 1). The peer CTA sees the same scores, so it
                     // takes the same decision. Waits for P.V of the previous tile first.
                     const int pb = int((i - 1) % kSBufs);
-                    if (!__all_sync(0xffffffffu, MLA_TW(7, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) / kSBufs) & 1),
-                                                                     abort, p.err, ERR_TIMEOUT_BASE + 8))))
+                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) / kSBufs) & 1), abort,
+                                                           p.err, ERR_TIMEOUT_BASE + 9)))
                         break;
                     tc_fence_after();
                     mt = fmaxf(mt, m_run);
                     const float alpha = ex2((m_run - mt) * c);
+#pragma unroll 1
                     for (int c32 = 0; c32 < kHalf / 32; ++c32) {
                         uint32_t o[32];
                         tmem_ld32(tmem + lane_off + kTmemO + c32 * 32, o);
@@ -526,7 +544,6 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     l_run *= alpha;
                     m_run = mt;
                 }
-                MLA_PROF(wacc[18] += clock64() - tph;)
                 const float mc = m_run * c;
                 uint32_t pk[NK / 2];
                 float ls = 0.f;
@@ -544,22 +561,19 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 }
                 l_run += ls;
                 __syncwarp();
-                MLA_PROF(const long long tst = clock64();)
-                tmem_st16(tmem + lane_off + kTmemS + sb * NK, pk);
+                tmem_st32(tmem + lane_off + kTmemS + sb * NK, pk);
                 tmem_st_wait();
-                MLA_PROF(wacc[19] += clock64() - tst;)
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
-                MLA_PROF(wacc[12] += clock64() - tph;)
                 if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 4);
                 if (last) {
-                    MLA_PROF(const long long tep = clock64();)
-                    if (!__all_sync(0xffffffffu, MLA_TW(8, mbar_wait(&bars->o_done[sb], uint32_t((i / kSBufs) & 1), abort,
-                                                                     p.err, ERR_TIMEOUT_BASE + 9))))
+                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
+                                                           ERR_TIMEOUT_BASE + 10)))
                         break;
                     tc_fence_after();
                     const int64_t slot = cl * p.max_segs + seg_local;
                     float* dst = p.O_part + (slot * kHeads + row) * kRank + rank * kHalf;
+#pragma unroll 1
                     for (int c32 = 0; c32 < kHalf / 32; ++c32) {
                         uint32_t o[32];
                         tmem_ld32(tmem + lane_off + kTmemO + c32 * 32, o);
@@ -575,120 +589,75 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     }
                     tc_fence_before();
                     ++seg_local;
-                    MLA_PROF(wacc[13] += clock64() - tep;)
                 }
-#pragma unroll
-                for (int e = 0; e < 32; ++e) sr_cur[e] = sr_next[e];
                 advance(p, it);
             }
-            MLA_PROF(wacc[14] = clock64() - t_loop0;)
         } else if (warp == 2 || warp == 3) {
           if constexpr (Tr::kConvert) {
             // ------------------------------------------------------------ fp32 -> bf16
-            // Converts two fp32 half-tile staging buffers into one bf16 128B-swizzled
-            // slot. Every thread reads its share of a half tile into registers and
+            // Converts four fp32 quarter-tile staging buffers into one bf16 slot.
+            // Every thread reads its share of a quarter tile into registers and
             // releases the staging buffer before writing, so the next TMA load can
             // start at once.
             const int ct = (warp - 2) * 32 + lane;
             // Lanes take consecutive 16-byte (4 x fp32) pieces of a staging row, so a
             // warp's shared-memory reads are dense; each piece becomes 8 bytes of bf16.
-            constexpr int kU = kStgRows * (kHalf / 4) / kConvThreads;   // c_kv float4 pieces per thread
-            constexpr int kP = kStgRows * (kRope / 4) / kConvThreads;   // pe float4 pieces per thread (CTA 1)
-            static_assert(kU * kConvThreads == kStgRows * (kHalf / 4) && kP * kConvThreads == kStgRows * (kRope / 4),
-                          "converter mapping");
-            // specialised per rank at compile time: CTA 1 also converts the rope dims
-            auto convert = [&](auto rope_tag) {
-                constexpr bool kR = decltype(rope_tag)::value;
-                bool okc = true;
-                for (int64_t i = 0; okc && i < n; ++i) {
-                    const int sl = int(i % Tr::kSlots);
-                    if (!MLA_TW(10, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                                              ERR_TIMEOUT_BASE + 11)))
+            constexpr int kU = kStgRows * (kHalf / 4) / kConvThreads;       // latent float4 pieces per thread
+            constexpr int kP = kStgRows * (kRopeHalf / 4) / kConvThreads;   // rope float4 pieces per thread
+            static_assert(kU * kConvThreads == kStgRows * (kHalf / 4) &&
+                          kP * kConvThreads == kStgRows * (kRopeHalf / 4), "converter mapping");
+            bool okc = true;
+            for (int64_t i = 0; okc && i < n; ++i) {
+                const int sl = int(i % Tr::kSlots);
+                if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                               ERR_TIMEOUT_BASE + 11))
+                    break;
+                if (ct == 0) trace_put(p, 3, i * 16 + 2);
+                unsigned char* buf = slots + sl * kSlotBytes;
+                for (int h = 0; h < NK / kStgRows; ++h) {
+                    const int64_t k = int64_t(NK / kStgRows) * i + h;
+                    const int st = int(k % Tr::kStages);
+                    if (!mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 12)) {
+                        okc = false;
                         break;
-                    if (ct == 0) trace_put(p, 3, i * 16 + 2);
-                    unsigned char* buf = slots + sl * kSlotBytes;
-                    for (int h = 0; h < 2; ++h) {
-                        const int64_t k = 2 * i + h;
-                        const int st = int(k % Tr::kStages);
-                        if (!MLA_TW(9, mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
-                                                 ERR_TIMEOUT_BASE + 10))) {
-                            okc = false;
-                            break;
-                        }
-                        MLA_PROF(long long tc0 = clock64();)
-                        const float4* src = reinterpret_cast<const float4*>(stg + st * kStgBytes);
-                        uint2 cv[kU], pv[kP];
-                        float4 a[kU], b[kP];
-                        // all loads of the half tile first, then the conversions
-    #pragma unroll
-                        for (int q = 0; q < kU; ++q) a[q] = src[ct + q * kConvThreads];
-                        if constexpr (kR) {
-    #pragma unroll
-                            for (int q = 0; q < kP; ++q) b[q] = src[kStgRows * (kHalf / 4) + ct + q * kConvThreads];
-                        }
-    #pragma unroll
-                        for (int q = 0; q < kU; ++q) cv[q] = make_uint2(pack_bf16(a[q].x, a[q].y), pack_bf16(a[q].z, a[q].w));
-                        if constexpr (kR) {
-    #pragma unroll
-                            for (int q = 0; q < kP; ++q) pv[q] = make_uint2(pack_bf16(b[q].x, b[q].y), pack_bf16(b[q].z, b[q].w));
-                        }
-                        MLA_PROF(wacc[16] += clock64() - tc0; tc0 = clock64();)
-                        // my generic-proxy reads of the staging buffer must be ordered before
-                        // the next TMA (async-proxy) write into it
-                        fence_proxy_async_smem();
-                        mbar_arrive(&bars->stg_empty[st]);
-                        MLA_PROF(wacc[17] += clock64() - tc0; tc0 = clock64();)
-    #pragma unroll
-                        for (int q = 0; q < kU; ++q) {
-                            const int f = ct + q * kConvThreads;          // float4 index in the half tile
-                            const int r = h * kStgRows + (f >> 6), c4 = f & 63;
-                            const int chunk = c4 >> 4, unit = ((c4 & 15) >> 1) ^ (r & 7);
-                            *reinterpret_cast<uint2*>(buf + chunk * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = cv[q];
-                        }
-                        if constexpr (kR) {
-    #pragma unroll
-                            for (int q = 0; q < kP; ++q) {
-                                const int f = ct + q * kConvThreads;
-                                const int r = h * kStgRows + (f >> 4), c4 = f & 15;
-                                const int unit = (c4 >> 1) ^ (r & 7);
-                                *reinterpret_cast<uint2*>(buf + 4 * kChunkBytes + r * 128 + unit * 16 + (c4 & 1) * 8) = pv[q];
-                            }
-                        }
-                        MLA_PROF(wacc[18] += clock64() - tc0;)
                     }
-                    if (!okc) break;
-                    MLA_PROF(const long long tf0 = clock64();)
+                    const float4* src = reinterpret_cast<const float4*>(stg + st * kStgBytes);
+                    float4 a[kU], b[kP];
+                    // all loads of the quarter tile first, then the conversions
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) a[q] = src[ct + q * kConvThreads];
+#pragma unroll
+                    for (int q = 0; q < kP; ++q) b[q] = src[kStgLatBytes / 16 + ct + q * kConvThreads];
+                    // my generic-proxy reads of the staging buffer must be ordered before
+                    // the next TMA (async-proxy) write into it
                     fence_proxy_async_smem();
-                    mbar_arrive(&bars->bf_full[sl]);
-                    MLA_PROF(wacc[19] += clock64() - tf0;)
+                    mbar_arrive(&bars->stg_empty[st]);
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        const int f = ct + q * kConvThreads;          // float4 index in the quarter tile
+                        const int r = h * kStgRows + (f >> 6), c4 = f & 63;
+                        *reinterpret_cast<uint2*>(buf + (c4 >> 4) * kChunkBytes +
+                                                  swz128(uint32_t(r), uint32_t((c4 & 15) >> 1)) + (c4 & 1) * 8) =
+                            make_uint2(pack_bf16(a[q].x, a[q].y), pack_bf16(a[q].z, a[q].w));
+                    }
+#pragma unroll
+                    for (int q = 0; q < kP; ++q) {
+                        const int f = ct + q * kConvThreads;
+                        const int r = h * kStgRows + (f >> 3), c4 = f & 7;
+                        *reinterpret_cast<uint2*>(buf + 4 * kChunkBytes + swz64(uint32_t(r), uint32_t(c4 >> 1)) +
+                                                  (c4 & 1) * 8) =
+                            make_uint2(pack_bf16(b[q].x, b[q].y), pack_bf16(b[q].z, b[q].w));
+                    }
                 }
-            };
-            if (rank == 1) convert(std::true_type{});
-            else convert(std::false_type{});
+                if (!okc) break;
+                fence_proxy_async_smem();
+                mbar_arrive(&bars->bf_full[sl]);
+            }
           }
         }
     }
 
-#ifdef MLA_TC_PROFILE
-    if (p.trace) {
-        const bool rep = (warp == 0 && lane == 0) || (warp == 1 && lane == 0) || (warp == 4 && lane == 0) ||
-                         (warp == 2 && lane == 0);
-        if (rep)
-            for (int k = 0; k < 15; ++k)
-                if (wacc[k]) trace_put(p, 8 + k, wacc[k] / 1000);
-        if (threadIdx.x == 0) trace_put(p, 23, (clock64() - t_kernel0) / 1000);
-        if (warp == 4 && lane == 0) {
-            trace_put(p, 26, wacc[18] / 1000);
-            trace_put(p, 27, wacc[19] / 1000);
-        }
-        if (warp == 1 && lane == 0) {
-            trace_put(p, 24, wacc[16] / 1000);
-            trace_put(p, 25, wacc[17] / 1000);
-        }
-        if (warp == 2 && lane == 0)
-            for (int k = 0; k < 4; ++k) trace_put(p, 28 + k, wacc[16 + k] / 1000);
-    }
-#endif
     if (threadIdx.x == 0) trace_put(p, 4, 1);
     tc_fence_before();
     __syncthreads();
@@ -763,9 +732,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+// 2-D map over a row-major [rows, cols] array; swizzle 0 (none), 64 or 128 bytes.
 template <typename T>
 bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint32_t box_cols, uint32_t box_rows,
-              bool swz) {
+              int swizzle) {
     auto fn = encode_fn();
     if (!fn) return false;
     const CUtensorMapDataType dt = std::is_same<T, float>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -776,7 +746,9 @@ bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint
     cuuint32_t box[2] = {box_cols, box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    swz ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    swizzle == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : swizzle == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -857,12 +829,15 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         p.max_segs = pl.max_segs;
         float* O_norm = reinterpret_cast<float*>(ws + pl.off_norm);
 
+        // fp32 storage: unswizzled quarter-tile boxes into staging (latent half, rope
+        // half); 16-bit storage: straight into the slots, 64-dim latent chunks with
+        // the 128-byte swizzle and the 32-dim rope half with the 64-byte swizzle
         CUtensorMap tm_ckv, tm_pe;
-        const bool swz = !Traits<T>::kConvert;
+        const bool direct = !Traits<T>::kConvert;
         const int64_t rows = a.batch * a.sk;
-        const uint32_t box_rows = swz ? uint32_t(NK) : uint32_t(kStgRows);
-        if (!make_map<T>(&tm_ckv, a.c_kv, rows, kRank, swz ? 64 : kHalf, box_rows, swz) ||
-            !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, 64, box_rows, swz))
+        const uint32_t box_rows = direct ? uint32_t(NK) : uint32_t(kStgRows);
+        if (!make_map<T>(&tm_ckv, a.c_kv, rows, kRank, direct ? 64 : kHalf, box_rows, direct ? 128 : 0) ||
+            !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, kRopeHalf, box_rows, direct ? 64 : 0))
             return set_error(MLA_ERR_CUDA, "MLA: cuTensorMapEncodeTiled failed (alignment of c_kv / pe_cache?)");
 
         auto kern = mla_decode_tc_kernel<T>;
@@ -907,11 +882,8 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                     (long long)(2 * pl.nclusters));
             for (int64_t b = 0; b < 2 * pl.nclusters; ++b) {
                 const volatile int* t = trace_host + b * 32;
-                fprintf(stderr, "  cta %2lld prod %d mma %d soft %d conv %d end %d sync %d exit %d | kcyc total %d "
-                        "stg_empty %d bf_empty(p) %d p_full %d q_ready %d bf_full %d s_full %d x_full %d o_resc %d "
-                        "o_last %d full(c) %d bf_empty(c) %d ld+send %d compute %d epi %d softloop %d pv_issue %d s_issue %d | cmp_pre %d p_store %d | conv ld %d fence1 %d st %d fence2 %d\n",
-                        (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6], t[23], t[8], t[9], t[10], t[11], t[12],
-                        t[13], t[14], t[15], t[16], t[17], t[18], t[19], t[20], t[21], t[22], t[24], t[25], t[26], t[27], t[28], t[29], t[30], t[31]);
+                fprintf(stderr, "  cta %3lld producer %d mma %d softmax %d converter %d end %d sync %d exit %d\n",
+                        (long long)b, t[0], t[1], t[2], t[3], t[4], t[5], t[6]);
             }
             // a kernel still running may write the buffer: keep it mapped (leaked) in that case
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");

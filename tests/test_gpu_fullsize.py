@@ -7,7 +7,13 @@ agreement the north-star correctness clause asks to report.
 Mirrors the reference's full-forward gate (run_scenario,
 exhaustive_benchmark_suite.py:467-484) and check_3d.py:36-44 at c1/c2/c3 sizes.
 
-Tolerances (rel-L2 against fp64): exact precision 1e-5, tensor precision 2e-2.
+Tolerances. Exact precision: rel-L2 <= 1e-5 against the reference's own path
+run in fp32 (the oracle in fp32, which is how the reference runs), and, against
+fp64, within 5x of that fp32 path's own error (check_3d.py:40-44). At these
+sizes the fp32 reference itself is ~1.4e-5 (c1) to ~3e-5 (c2) away from fp64,
+mostly from its fp32 RoPE angles at positions up to Sk (pos * inv_freq rounded
+to fp32, exhaustive_benchmark_suite.py:215-220), so a bare 1e-5 bound against
+fp64 would fail the reference too. Tensor precision: rel-L2 <= 2e-2 against fp64.
 argmax agreement: the key with the largest score per (sequence, query, head),
 computed in fp64 from the path's own Q-prep output (and, in tensor precision,
 from the bf16-rounded query and cache the tensor-core kernel multiplies), must
@@ -50,9 +56,9 @@ def _sample(B: int):
     return sorted({0, B // 2, B - 1})
 
 
-def _oracle_seq(t, b, w):
-    """fp64 oracle for sequence b: (out, q_absorbed, q_rope)."""
-    s = {k: (v.double() if v.is_floating_point() else v) for k, v in t.items()}
+def _oracle_seq(t, b, w, dtype=torch.float64):
+    """Oracle in `dtype` for sequence b: (out, q_absorbed, q_rope)."""
+    s = {k: (v.to(dtype) if v.is_floating_point() else v) for k, v in t.items()}
     qa, qr = orc.q_absorbed(s["x"][b:b + 1], s["W_q_a"], s["q_norm_w"], s["W_q_b"], s["W_uk"], s["positions"])
     out = orc.mla_attention(qa, qr, s["c_kv"][b:b + 1], s["pe_cache"][b:b + 1], s["W_uv"], w.scale, w.causal)
     return out, qa, qr
@@ -85,16 +91,24 @@ def test_full_layer_forward_vs_oracle(mcc, cfg, precision):
     g = {k: v.to(DEV) for k, v in t.items()}
     out, qa, qr = _layer(mcc, g, w, precision)
     assert out.shape == (w.batch, w.sq, w.heads, w.v_dim) and torch.isfinite(out).all()
-    errs, agree = [], []
+    errs, errs32, noise, agree = [], [], [], []
     for b in _sample(w.batch):
         ref, rqa, rqr = _oracle_seq(t, b, w)
+        ref32, _, _ = _oracle_seq(t, b, w, torch.float32)
         errs.append(rel_l2(out[b:b + 1].cpu(), ref))
+        errs32.append(rel_l2(out[b:b + 1].cpu(), ref32))
+        noise.append(rel_l2(ref32, ref))
         agree.append(argmax_agreement(qa[b:b + 1].cpu(), qr[b:b + 1].cpu(), t["c_kv"][b:b + 1],
                                       t["pe_cache"][b:b + 1], rqa, rqr, t["c_kv"][b:b + 1], t["pe_cache"][b:b + 1],
                                       w, bf16=(precision == "tensor")))
-    print(f"{cfg} {precision}: rel-L2 per sampled sequence {['%.2e' % e for e in errs]}, "
+    print(f"{cfg} {precision}: rel-L2 vs fp64 {['%.2e' % e for e in errs]}, vs the fp32 reference path "
+          f"{['%.2e' % e for e in errs32]}, fp32 reference vs fp64 {['%.2e' % e for e in noise]}, "
           f"argmax agreement {['%.4f' % a for a in agree]}")
-    assert max(errs) < TOL[precision], errs
+    if precision == "exact":
+        assert max(errs32) < 1e-5, errs32
+        assert all(e < 5 * max(n, 1e-7) for e, n in zip(errs, noise)), (errs, noise)
+    else:
+        assert max(errs) < TOL[precision], errs
     assert min(agree) >= ARGMAX_MIN[precision], agree
     del g
     torch.cuda.empty_cache()
@@ -107,10 +121,15 @@ def test_exact_q_absorbed_b128_vs_oracle(mcc):
     g = {k: t[k].to(DEV) for k in ("x", "W_q_a", "q_norm_w", "W_q_b", "W_uk", "positions")}
     qa, qr = mcc.q_absorbed_ex(g["x"], g["W_q_a"], g["q_norm_w"], g["W_q_b"], g["W_uk"], g["positions"],
                                w.nope, w.rope, mc.EPS, precision="exact")
+    ra, rr = orc.q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"])   # fp32
     s = {k: (v.double() if v.is_floating_point() else v) for k, v in t.items()}
-    ra, rr = orc.q_absorbed(s["x"], s["W_q_a"], s["q_norm_w"], s["W_q_b"], s["W_uk"], s["positions"])
+    ra64, rr64 = orc.q_absorbed(s["x"], s["W_q_a"], s["q_norm_w"], s["W_q_b"], s["W_uk"], s["positions"])
     assert rel_l2(qa.cpu(), ra) < 1e-5
     assert rel_l2(qr.cpu(), rr) < 1e-5
+    # against fp64: q_absorbed at fp32 accuracy; q_rope within 2x of the fp32 path's
+    # own RoPE-angle error at position Sk
+    assert rel_l2(qa.cpu(), ra64) < 1e-5
+    assert rel_l2(qr.cpu(), rr64) < 2 * rel_l2(rr, rr64)
 
 
 @pytest.mark.parametrize("precision", ["exact", "tensor"])
