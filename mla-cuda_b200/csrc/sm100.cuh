@@ -139,6 +139,20 @@ __device__ __forceinline__ uint32_t nclusters_x() {
     asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
     return r;
 }
+// Per-warpgroup register budget changes (all warps of the warpgroup execute
+// them together). An increase waits until registers released by decreases in
+// other warpgroups of the CTA are available.
+template <uint32_t N> __device__ __forceinline__ void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N> __device__ __forceinline__ void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -158,6 +172,13 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, float a, float
                                             uint32_t remote_bar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
                  ::"r"(remote_addr), "f"(a), "f"(b), "f"(c), "f"(d), "r"(remote_bar) : "memory");
+}
+
+// 4-byte form: also used as a cheap remote signal (its byte count completes a
+// phase of the peer's barrier; no cluster-scope release is involved).
+__device__ __forceinline__ void st_async_b32(uint32_t remote_addr, float v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                 ::"r"(remote_addr), "r"(__float_as_uint(v)), "r"(remote_bar) : "memory");
 }
 
 // ----------------------------------------------------------------- tcgen05
@@ -271,6 +292,20 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
+}
+
+// bf16 round-to-nearest-even on the integer pipe (the XU pipe that cvt uses is
+// the decode kernel's scarcest unit): adding 0x7FFF plus the lowest kept bit
+// carries into bit 16 exactly when the discarded half is above one half ULP,
+// or equal to it with an odd kept part. Identical to cvt.rn.bf16.f32 for every
+// input except signalling NaNs whose payload sits only in the low 16 bits
+// (those become infinities).
+__device__ __forceinline__ uint32_t bf16_rn_hi(float x) {
+    const uint32_t u = __float_as_uint(x);
+    return u + 0x7FFFu + ((u >> 16) & 1u);   // bf16 bits in the upper half
+}
+__device__ __forceinline__ uint32_t pack_bf16_int(float lo, float hi) {
+    return __byte_perm(bf16_rn_hi(lo), bf16_rn_hi(hi), 0x7632);
 }
 
 __device__ __forceinline__ float ex2(float x) {

@@ -65,7 +65,7 @@ constexpr int kRank = 512;
 constexpr int kRope = 64;
 constexpr int kHalf = 256;                  // latent dims per CTA
 constexpr int kRopeHalf = 32;               // rope dims per CTA
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 constexpr int kConvThreads = 64;            // fp32 -> bf16 converter threads (warps 2, 3)
 constexpr int kChunkBytes = NK * 128;       // 64 latent dims of a tile: 64 rows of 128 B, 128B swizzle
 constexpr int kRopeChunkBytes = NK * 64;    // 32 rope dims of a tile: 64 rows of 64 B, 64B swizzle
@@ -74,7 +74,10 @@ constexpr int kStgRows = 16;                // an fp32 staging buffer holds a qu
 constexpr int kStgLatBytes = kStgRows * kHalf * 4;
 constexpr int kStgBytes = kStgRows * (kHalf + kRopeHalf) * 4;
 constexpr int kXBufs = 2;                   // partial-score exchange buffers (flow-controlled)
-constexpr int kXBytes = kHeads * NK * 4;    // one buffer: 128 rows x 64 fp32, 16-byte chunks XOR-swizzled by row
+// one exchange buffer: the 128 rows x 64 fp32 partial scores of a tile, stored
+// chunk-major (16-byte chunk e of row r at (e*128 + r)*16), so that a warp's 32
+// rows write and read 512 contiguous bytes per instruction
+constexpr int kXBytes = kHeads * NK * 4;
 constexpr int kQRopeBytes = kHeads * kRopeHalf * 2;   // rope query slice: 128 rows of 64 B, 64B swizzle
 
 // TMEM columns: O half, kSBufs score / probability buffers, the query slice.
@@ -113,7 +116,7 @@ template <> struct Traits<__half> {
 template <typename T>
 constexpr size_t smem_bytes() {
     return 1024 /*align slack*/ + size_t(Traits<T>::kSlots) * kSlotBytes + size_t(Traits<T>::kStages) * kStgBytes +
-           kXBufs * size_t(kXBytes) + kQRopeBytes + 1024 /*barriers*/;
+           kXBufs * size_t(kXBytes) + kQRopeBytes + 4096 /*barriers, row maxima, row sums*/;
 }
 static_assert(smem_bytes<float>() <= 232448 && smem_bytes<__nv_bfloat16>() <= 232448, "shared memory budget");
 
@@ -124,6 +127,7 @@ struct Params {
     float* ml;          // [slots, 128, 2]  (running max in log2 units, sum)
     int* err;
     int* trace;         // debug only (MLA_TC_TRACE): per-CTA progress words in mapped host memory
+    long long* prof;    // debug only (MLA_TC_PROFILE builds): [grid][kProfSlots] cycle counters
     int64_t batch, sq, sk;
     int causal;
     float c_log2;       // log2(e) / scale
@@ -140,6 +144,19 @@ __device__ __forceinline__ int64_t group_keys(const Params& p, int64_t g) {
 __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
     return (group_keys(p, g) + NK - 1) / NK;
 }
+
+// Debug cycle accounting (compiled in with -DMLA_TC_PROFILE, printed by the host
+// when MLA_TC_PROF is set): clock64 cycles spent in each wait site (slot = the
+// site's timeout code - 100) and in a few work phases, summed per CTA.
+#ifdef MLA_TC_PROFILE
+#define MLA_TW(slot, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); \
+    wacc[slot] += clock64() - _t0; return _r; }())
+#define MLA_PROF(stmt) stmt
+#else
+#define MLA_TW(slot, expr) (expr)
+#define MLA_PROF(stmt)
+#endif
+constexpr int kProfSlots = 24;
 
 __device__ __forceinline__ void trace_put(const Params& p, int role, int64_t v) {
     if (p.trace) *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 32 + role) = int(v);
@@ -187,12 +204,17 @@ struct Bars {
     uint64_t p_full[kSBufs];
     uint64_t o_done[kSBufs];
     uint64_t x_full[kXBufs][4];   // per softmax warp: peer's partial scores arrived (st.async byte count)
-    uint64_t x_free[kXBufs][4];   // per softmax warp: the peer has read my push into its buffer
+    uint64_t x_free[kXBufs][4];   // per exchange warp: the peer has read my previous push into its buffer
+                                  // (completed by a 4-byte st.async from the peer's softmax warp)
+    float sink[kXBufs][4];        // landing words of those 4-byte signals
+    float xmax[2][2 * kHeads];    // per tile parity: the two softmax warps' half-tile row maxima
+    float xl[2 * kHeads];         // epilogue: the two softmax warps' partial row sums
+    uint64_t s_read[kSBufs];      // the exchange warps have read my partial scores of the buffer
     uint64_t q_ready;
     uint32_t tmem_base;
     int abort;
 };
-static_assert(sizeof(Bars) <= 1024, "barrier area");
+static_assert(sizeof(Bars) <= 4096, "barrier area");
 
 // 64B-swizzled byte offset of 16-byte unit u (0..3) of row r in a region of
 // 64-byte rows (the layout TMA's SWIZZLE_64B writes and the MMA descriptor's
@@ -222,6 +244,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     const int64_t t_end = min(t_begin + p.tiles_per_cluster, p.total_tiles);
     const int64_t n = t_end > t_begin ? t_end - t_begin : 0;   // tiles of this cluster
     volatile int* abort = &bars->abort;
+    MLA_PROF(long long wacc[kProfSlots] = {0};)
+    MLA_PROF(const long long t_kernel0 = clock64();)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 6; ++i) {
@@ -232,15 +256,23 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
         }
         for (int i = 0; i < kSBufs; ++i) {
             mbar_init(&bars->s_full[i], 1);
-            mbar_init(&bars->p_full[i], 128);
+            mbar_init(&bars->p_full[i], 256);
             mbar_init(&bars->o_done[i], 1);
         }
+        for (int i = 0; i < kSBufs; ++i) mbar_init(&bars->s_read[i], 128);
         for (int i = 0; i < kXBufs; ++i)
             for (int w = 0; w < 4; ++w) {
                 mbar_init(&bars->x_full[i][w], 1);
                 mbar_init(&bars->x_free[i][w], 1);
             }
         mbar_init(&bars->q_ready, 128);
+        // the bytes the peer pushes for tiles 0 and 1 (later tiles are announced by
+        // the softmax warp that consumed the buffer's previous tile)
+        for (int i = 0; i < kXBufs; ++i)
+            for (int w = 0; w < 4; ++w) {
+                mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(32 * NK * 4));
+                mbar_arrive_expect_tx(&bars->x_free[i][w], 4u);   // the signal freeing the buffer for tile i+2
+            }
         bars->abort = 0;
         fence_mbar_init();
     }
@@ -255,6 +287,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     cluster_sync();   // the peer's barriers exist before any remote arrive
     const uint32_t tmem = bars->tmem_base;
 
+    // Register split per warpgroup (launched with 128 per thread, 512 threads),
+    // set at the top of each role: the exchange warps (warpgroup 2) give 40
+    // back, the softmax warpgroups (1 and 3) take 16 more each; warpgroup 0 (TMA,
+    // MMA, converters) keeps 128. 128 + 144 + 88 + 144 = 504 <= 4 x 128.
     if (n > 0) {
         if (warp == 0 && lane == 0) {
             // ------------------------------------------------------------ TMA producer
@@ -267,8 +303,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     for (int h = 0; h < NK / kStgRows && okp; ++h) {
                         const int64_t k = int64_t(NK / kStgRows) * i + h;
                         const int st = int(k % Tr::kStages);
-                        okp = mbar_wait(&bars->stg_empty[st], uint32_t(((k / Tr::kStages) & 1) ^ 1), abort, p.err,
-                                        ERR_TIMEOUT_BASE + 1);
+                        okp = MLA_TW(1, mbar_wait(&bars->stg_empty[st], uint32_t(((k / Tr::kStages) & 1) ^ 1), abort, p.err,
+                                        ERR_TIMEOUT_BASE + 1));
                         if (!okp) break;
                         unsigned char* dst = stg + st * kStgBytes;
                         mbar_arrive_expect_tx(&bars->full[st], uint32_t(kStgBytes));
@@ -279,8 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     if (!okp) break;
                 } else {
                     const int sl = int(i % Tr::kSlots);
-                    if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                                   ERR_TIMEOUT_BASE + 2))
+                    if (!MLA_TW(2, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 2)))
                         break;
                     unsigned char* dst = slots + sl * kSlotBytes;
                     mbar_arrive_expect_tx(&bars->full[sl], uint32_t(kSlotBytes));
@@ -310,9 +346,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 // stride between 8-key groups). Releases the slot, signals o_done.
                 auto issue_pv = [&](int64_t i, bool first) -> bool {
                     const int sb = int(i % kSBufs);
-                    if (!mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3))
+                    if (!MLA_TW(3, mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3)))
                         return false;
                     tc_fence_after();
+                    MLA_PROF(const long long t_pv = clock64();)
                     const int sl = int(i % Tr::kSlots);
                     const uint32_t base = smem_slots + sl * kSlotBytes;
                     const uint32_t p_tmem = tmem + kTmemS + sb * NK;
@@ -323,24 +360,30 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                                (first && k == 0) ? 0u : 1u);
                     mma_commit(&bars->bf_empty[sl]);
                     mma_commit(&bars->o_done[sb]);
+                    MLA_PROF(wacc[17] += clock64() - t_pv;)
                     return true;
                 };
                 for (int64_t i = 0; i < n && ok; ++i) {
                     const bool first = (i == 0) || it.j == 0;
                     if (first) {
-                        if (!mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4)) break;
+                        if (!MLA_TW(4, mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4))) break;
                         ++seg;
                     }
                     const int sl = int(i % Tr::kSlots);
                     trace_put(p, 1, i * 16 + 1);
                     uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
-                    if (!mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5)) break;
+                    if (!MLA_TW(5, mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5))) break;
+                    const int sb = int(i % kSBufs);
+                    // the exchange warps have read my partial of tile i-2 from this buffer
+                    if (i >= kSBufs && !MLA_TW(13, mbar_wait(&bars->s_read[sb], uint32_t(((i - kSBufs) / kSBufs) & 1),
+                                                            abort, p.err, ERR_TIMEOUT_BASE + 13)))
+                        break;
                     tc_fence_after();
                     const uint32_t base = smem_slots + sl * kSlotBytes;
-                    const int sb = int(i % kSBufs);
                     // B = K [64 keys x 16 dims], K-major: latent chunk k/4 (128B swizzle,
                     // +32 B per k-step), then the rope chunk (64B swizzle, +32 B per
                     // k-step) against the rope query slice in shared memory.
+                    MLA_PROF(const long long t_si = clock64();)
                     const uint64_t bd0 = smem_desc(base, 16, 1024, 2);
                     const uint64_t rd0 = smem_desc(base + 4 * kChunkBytes, 16, 512, 4);
                     const uint32_t d_s = tmem + kTmemS + sb * NK;
@@ -352,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     for (int k = 0; k < kRopeHalf / 16; ++k)
                         mma_ss(d_s, qd0 + uint64_t((k * 32) >> 4), rd0 + uint64_t((k * 32) >> 4), idesc_s, 1u);
                     mma_commit(&bars->s_full[sb]);
+                    MLA_PROF(wacc[16] += clock64() - t_si;)
                     trace_put(p, 1, i * 16 + 2);
                     if (i >= 1) ok = issue_pv(i - 1, prev_first);
                     prev_first = first;
@@ -359,31 +403,26 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 }
                 if (ok && n > 0) issue_pv(n - 1, prev_first);
             }
-        } else if (warp >= 4 && warp < 8) {
-            // ------------------------------------------------------------ softmax
-            // Pipelined one tile ahead: iteration i first "prepares" tile i+1 (loads
-            // the next segment's query if one starts, waits for its partial scores,
-            // pushes them to the peer) and then finishes tile i (reloads its own
-            // partial from TMEM, adds the peer's, online softmax, P to TMEM,
-            // epilogue), so the DSMEM round trip of tile i+1 overlaps the softmax
-            // of tile i. Exchange buffer b (= tile % 2) of this warp's 32 rows is
-            // pushed into by the peer's matching warp only after this warp has told
-            // it (x_free) that it read the buffer's previous tile.
-            const int row = threadIdx.x - 128;               // head
+        } else if (warp >= 8 && warp < 12) {
+            setmaxnreg_dec<88>();
+            // ------------------------------------------------------------ exchange
+            // Per tile: loads the next segment's query when one starts (latent slice
+            // into TMEM, rope slice into shared memory), waits for my partial scores,
+            // and pushes them into the peer's exchange buffer with st.async (bytes
+            // counted on the peer's barrier). Exchange buffer b (= tile % 2) of a
+            // warp's 32 rows is pushed into only after the peer's matching softmax
+            // warp has said (x_free) that it read the buffer's previous tile. Runs
+            // ahead of the softmax warps, so the DSMEM transfer is off their path.
+            const int row = threadIdx.x - 256;               // head
             const int wq = warp & 3;
             const uint32_t lane_off = uint32_t(wq * 32) << 16;
-            const float c = p.c_log2;
-            const float tau = 8.0f / c;                      // lazy rescale threshold (raw units)
-            const uint32_t sw = uint32_t(row & 7);            // chunk swizzle of my exchange row
-            // peer addresses of my exchange row and of my warp's exchange barriers
-            // (buffer 0; buffer b is at +b*kXBytes / +b*4*8 bytes)
-            const uint32_t xpeer0 = map_peer(xbuf + row * NK, peer);
+            // peer addresses of my exchange row (chunk 0) and of my warp's exchange
+            // barriers (buffer 0; buffer b is at +b*kXBytes / +b*4*8 bytes)
+            const uint32_t xpeer0 = map_peer(xbuf + row * 4, peer);
             const uint32_t xbar_peer0 = map_peer(&bars->x_full[0][wq], peer);
-            int64_t seg_local = 0;
-            float m_run = -INFINITY, l_run = 0.f;
-            bool ok = true;
-
-            auto prepare = [&](int64_t i, const TileIter& itp) __attribute__((always_inline)) -> bool {
+            TileIter itp = locate(p, t_begin);
+            for (int64_t i = 0; i < n; ++i, advance(p, itp)) {
+                MLA_PROF(const long long t_pr = clock64();)
                 const bool first = (i == 0) || itp.j == 0;
                 const int sb = int(i % kSBufs);
                 if (first) {
@@ -437,21 +476,20 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     tc_fence_before();
                     mbar_arrive(&bars->q_ready);
                 }
-                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 1);
                 // every lane polls, then the warp reconverges: tcgen05.ld is warp-collective
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
-                                                       ERR_TIMEOUT_BASE + 6)))
-                    return false;
+                if (!__all_sync(0xffffffffu, MLA_TW(6, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
+                                                       ERR_TIMEOUT_BASE + 6))))
+                    break;
                 tc_fence_after();
                 const int xb = int(i % kXBufs);
                 const int64_t k = i / kXBufs;
-                // the peer's buffer xb must no longer hold tile i-2 unread
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_free[xb][wq], uint32_t((k & 1) ^ 1), abort, p.err,
-                                                       ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true)))
-                    return false;
-                // lane 0 announces the bytes the peer will push into my buffer for tile
-                // i; then st.async pushes my partial, counted on the peer's barrier
-                if (lane == 0) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 4));
+                // the peer's buffer xb must no longer hold tile i-2 unread; once it is
+                // free, arm the barrier for the signal that frees it for tile i+2
+                if (!__all_sync(0xffffffffu, MLA_TW(7, mbar_wait(&bars->x_free[xb][wq], uint32_t((k & 1) ^ 1), abort, p.err,
+                                                       ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true))))
+                    break;
+                if (lane == 0 && i >= kXBufs && i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_free[xb][wq], 4u);
+                // st.async pushes my partial, counted on the peer's barrier
 #pragma unroll
                 for (int h = 0; h < NK / 32; ++h) {   // 32 keys at a time
                     uint32_t sr[32];
@@ -459,99 +497,139 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     tmem_ld_wait();
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
-                        st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + ((uint32_t(h * 8 + e) ^ sw) << 4),
+                        st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + uint32_t(h * 8 + e) * (kHeads * 16),
                                     __uint_as_float(sr[4 * e]), __uint_as_float(sr[4 * e + 1]),
                                     __uint_as_float(sr[4 * e + 2]), __uint_as_float(sr[4 * e + 3]),
                                     xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
                 }
-                if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 3);
-                return true;
-            };
-
-            TileIter it = locate(p, t_begin);     // tile being finished
-            TileIter itn = it;                     // tile being prepared
-            ok = prepare(0, itn);
-            for (int64_t i = 0; i < n && ok; ++i) {
+                tc_fence_before();
+                mbar_arrive(&bars->s_read[sb]);
+                MLA_PROF(wacc[19] += clock64() - t_pr;)
+            }
+        } else if ((warp >= 4 && warp < 8) || warp >= 12) {
+            setmaxnreg_inc<144>();
+            // ------------------------------------------------------------ softmax
+            // Two warps per TMEM lane quarter: warps 4-7 take keys 0-31 of every
+            // tile, warps 12-15 keys 32-63. Per tile each warp adds my partial scores
+            // (TMEM) and the peer's (exchange buffer) for its 32 keys, and the two
+            // warps of a quarter swap their row maxima through shared memory (named
+            // barrier 1 + quarter), so both hold the same tile maximum, take the same
+            // lazy-rescale decision and share one running maximum. Each writes its
+            // half of P, keeps its own partial row sum, rescales and stores its 128
+            // columns of the O half; the sums are added at the epilogue. After both
+            // have read the exchange buffer, the first warp announces the bytes of
+            // the buffer's next tile and tells the peer's exchange warp (a 4-byte
+            // st.async completing its x_free barrier) that it may push them.
+            const int wq = warp & 3;
+            const int hk = warp >= 12 ? 1 : 0;                // key half
+            const int row = wq * 32 + lane;                  // head
+            const uint32_t lane_off = uint32_t(wq * 32) << 16;
+            const uint32_t bar_id = 1u + uint32_t(wq);
+            const float c = p.c_log2;
+            const float tau = 8.0f / c;                      // lazy rescale threshold (raw units)
+            // peer addresses of this quarter's x_free barrier and landing word
+            // (buffer 0; buffer b is at +b*4*8 / +b*4*4 bytes)
+            const uint32_t xfree_peer0 = map_peer(&bars->x_free[0][wq], peer);
+            const uint32_t sink_peer0 = map_peer(&bars->sink[0][wq], peer);
+            int64_t seg_local = 0;
+            float m_run = -INFINITY, l_run = 0.f;            // l_run: sum over my key half
+            TileIter it = locate(p, t_begin);
+            for (int64_t i = 0; i < n; ++i) {
                 const bool first = (i == 0) || it.j == 0;
                 const bool last = (i + 1 == n) || (it.j + 1 == it.tiles);
                 const int sb = int(i % kSBufs);
-                if (i + 1 < n) {
-                    advance(p, itn);
-                    if (!prepare(i + 1, itn)) break;
-                }
                 if (first) {
                     m_run = -INFINITY;
                     l_run = 0.f;
                 }
-                const int xb = int(i % kXBufs);
-                if (!__all_sync(0xffffffffu, mbar_wait(&bars->x_full[xb][wq], uint32_t((i / kXBufs) & 1), abort, p.err,
-                                                       ERR_TIMEOUT_BASE + 8, /*cluster_scope=*/true)))
+                if (!__all_sync(0xffffffffu, MLA_TW(14, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort,
+                                                                  p.err, ERR_TIMEOUT_BASE + 14))))
                     break;
-                // my partial of tile i, reloaded from TMEM (the buffer is not reused
-                // before P.V(i) is issued), plus the peer's partial
-                float s[NK];
-                {
-                    uint32_t* su = reinterpret_cast<uint32_t*>(s);
-                    tmem_ld32(tmem + lane_off + kTmemS + sb * NK, *reinterpret_cast<uint32_t(*)[32]>(&su[0]));
-                    tmem_ld32(tmem + lane_off + kTmemS + sb * NK + 32, *reinterpret_cast<uint32_t(*)[32]>(&su[32]));
-                }
-                const float* xr = xbuf + xb * (kHeads * NK) + row * NK;
+                tc_fence_after();
+                const int xb = int(i % kXBufs);
+                if (!__all_sync(0xffffffffu, MLA_TW(8, mbar_wait(&bars->x_full[xb][wq], uint32_t((i / kXBufs) & 1), abort,
+                                                                 p.err, ERR_TIMEOUT_BASE + 8, /*cluster_scope=*/true))))
+                    break;
+                // my partial of my 32 keys (the score buffer is not reused before P.V(i)
+                // is issued) plus the peer's partial
+                MLA_PROF(const long long t_fi = clock64();)
+                float s[32];
+                tmem_ld32(tmem + lane_off + kTmemS + sb * NK + hk * 32, *reinterpret_cast<uint32_t(*)[32]>(s));
+                const float* xr = xbuf + xb * (kHeads * NK) + row * 4;
                 tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < NK / 4; ++e) {
-                    const float4 pv = *reinterpret_cast<const float4*>(xr + ((e ^ int(sw)) << 2));
+                for (int e = 0; e < 8; ++e) {
+                    const float4 pv = *reinterpret_cast<const float4*>(xr + (hk * 8 + e) * (kHeads * 4));
                     s[4 * e] += pv.x;
                     s[4 * e + 1] += pv.y;
                     s[4 * e + 2] += pv.z;
                     s[4 * e + 3] += pv.w;
                 }
-                // my reads of the exchange buffer are done: the peer may push tile i+2
-                __syncwarp();
-                if (lane == 0) mbar_arrive_remote(&bars->x_free[xb][wq], peer);
-                const int64_t key0 = it.j * NK;
-                if (key0 + NK > it.keys) {            // ragged last tile of a group (warp-uniform)
+                MLA_PROF(wacc[20] += clock64() - t_fi; const long long t_f1 = clock64();)
+                const int64_t key0 = it.j * NK + hk * 32;
+                if (key0 + 32 > it.keys) {            // ragged last tile of a group (warp-uniform)
                     const int valid = int(it.keys - key0);
 #pragma unroll
-                    for (int e = 0; e < NK; ++e)
+                    for (int e = 0; e < 32; ++e)
                         if (e >= valid) s[e] = -INFINITY;
                 }
-                float mt = -INFINITY;
+                float m4[4];
 #pragma unroll
-                for (int e = 0; e < NK; ++e) mt = fmaxf(mt, s[e]);
+                for (int q = 0; q < 4; ++q) m4[q] = fmaxf(fmaxf(s[q], s[q + 4]), fmaxf(s[q + 8], s[q + 12]));
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    m4[q] = fmaxf(m4[q], fmaxf(fmaxf(s[q + 16], s[q + 20]), fmaxf(s[q + 24], s[q + 28])));
+                const float mh = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+                // swap half maxima with the other warp of this quarter (double-buffered
+                // by tile parity: my next write follows the next barrier, which the
+                // other warp reaches only after reading this one)
+                float* xm = reinterpret_cast<float*>(bars->xmax[i & 1]);
+                xm[hk * kHeads + row] = mh;
+                named_bar_sync(bar_id, 64);
+                float mt = fmaxf(mh, xm[(hk ^ 1) * kHeads + row]);
+                // Both warps have read the exchange buffer (each passed the barrier after
+                // a maximum that depends on every value it read): announce the bytes of
+                // the buffer's next tile (i+2) and free it for the peer's push.
+                if (hk == 0 && lane == 0) {
+                    if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 4));
+                    st_async_b32(sink_peer0 + uint32_t(xb) * 16u, mt, xfree_peer0 + uint32_t(xb) * 32u);
+                }
                 if (first) {
                     m_run = mt;
                 } else if (__any_sync(0xffffffffu, mt > m_run + tau)) {
-                    // Lazy rescale: the decision is per warp, because the TMEM accesses
-                    // below are warp-collective. Every lane of the warp moves to its own
-                    // new maximum (alpha <= 1). The peer CTA sees the same scores, so it
-                    // takes the same decision. Waits for P.V of the previous tile first.
+                    // Lazy rescale, decided per quarter (both warps see the same maxima;
+                    // the peer CTA sees the same scores, so it decides the same): every
+                    // row moves to its new maximum (alpha <= 1). Waits for P.V of the
+                    // previous tile first; each warp rescales its 128 O columns.
                     const int pb = int((i - 1) % kSBufs);
-                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) / kSBufs) & 1), abort,
-                                                           p.err, ERR_TIMEOUT_BASE + 9)))
+                    if (!__all_sync(0xffffffffu, MLA_TW(9, mbar_wait(&bars->o_done[pb], uint32_t(((i - 1) / kSBufs) & 1),
+                                                                     abort, p.err, ERR_TIMEOUT_BASE + 9))))
                         break;
                     tc_fence_after();
                     mt = fmaxf(mt, m_run);
                     const float alpha = ex2((m_run - mt) * c);
 #pragma unroll 1
-                    for (int c32 = 0; c32 < kHalf / 32; ++c32) {
+                    for (int c32 = 0; c32 < kHalf / 64; ++c32) {
                         uint32_t o[32];
-                        tmem_ld32(tmem + lane_off + kTmemO + c32 * 32, o);
+                        const uint32_t col = kTmemO + hk * (kHalf / 2) + c32 * 32;
+                        tmem_ld32(tmem + lane_off + col, o);
                         tmem_ld_wait();
                         for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-                        tmem_st32(tmem + lane_off + kTmemO + c32 * 32, o);
+                        tmem_st32(tmem + lane_off + col, o);
                     }
                     tmem_st_wait();
                     l_run *= alpha;
                     m_run = mt;
                 }
+                MLA_PROF(wacc[21] += clock64() - t_f1; const long long t_f2 = clock64();)
                 const float mc = m_run * c;
-                uint32_t pk[NK / 2];
-                float ls = 0.f;
+                uint32_t pk[16];
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int e = 0; e < NK; e += 2) {
+                for (int e = 0; e < 32; e += 2) {
                     const float p0 = ex2(fmaf(s[e], c, -mc));
                     const float p1 = ex2(fmaf(s[e + 1], c, -mc));
-                    ls += p0 + p1;
+                    ls[(e >> 1) & 3] += p0 + p1;
                     if constexpr (Tr::kFmt == 0) {
                         __half2 h2 = __floats2half2_rn(p0, p1);
                         pk[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
@@ -559,33 +637,39 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                         pk[e / 2] = pack_bf16(p0, p1);
                     }
                 }
-                l_run += ls;
+                l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                MLA_PROF(wacc[22] += clock64() - t_f2; const long long t_f3 = clock64();)
                 __syncwarp();
-                tmem_st32(tmem + lane_off + kTmemS + sb * NK, pk);
+                tmem_st16(tmem + lane_off + kTmemS + sb * NK + hk * 16, pk);
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
+                MLA_PROF(wacc[23] += clock64() - t_f3;)
+                MLA_PROF(wacc[18] += clock64() - t_fi;)
                 if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 4);
                 if (last) {
-                    if (!__all_sync(0xffffffffu, mbar_wait(&bars->o_done[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
-                                                           ERR_TIMEOUT_BASE + 10)))
+                    if (!__all_sync(0xffffffffu, MLA_TW(10, mbar_wait(&bars->o_done[sb], uint32_t((i / kSBufs) & 1), abort,
+                                                                      p.err, ERR_TIMEOUT_BASE + 10))))
                         break;
                     tc_fence_after();
                     const int64_t slot = cl * p.max_segs + seg_local;
-                    float* dst = p.O_part + (slot * kHeads + row) * kRank + rank * kHalf;
+                    float* dst = p.O_part + (slot * kHeads + row) * kRank + rank * kHalf + hk * (kHalf / 2);
 #pragma unroll 1
-                    for (int c32 = 0; c32 < kHalf / 32; ++c32) {
+                    for (int c32 = 0; c32 < kHalf / 64; ++c32) {
                         uint32_t o[32];
-                        tmem_ld32(tmem + lane_off + kTmemO + c32 * 32, o);
+                        tmem_ld32(tmem + lane_off + kTmemO + hk * (kHalf / 2) + c32 * 32, o);
                         tmem_ld_wait();
                         float4* d4 = reinterpret_cast<float4*>(dst + c32 * 32);
                         for (int e = 0; e < 8; ++e)
                             d4[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
                                                 __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
                     }
-                    if (rank == 0) {
+                    // the row sum is the sum of the two halves' sums
+                    bars->xl[hk * kHeads + row] = l_run;
+                    named_bar_sync(bar_id, 64);
+                    if (rank == 0 && hk == 0) {
                         p.ml[(slot * kHeads + row) * 2] = m_run * c;
-                        p.ml[(slot * kHeads + row) * 2 + 1] = l_run;
+                        p.ml[(slot * kHeads + row) * 2 + 1] = l_run + bars->xl[kHeads + row];
                     }
                     tc_fence_before();
                     ++seg_local;
@@ -609,19 +693,20 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
             bool okc = true;
             for (int64_t i = 0; okc && i < n; ++i) {
                 const int sl = int(i % Tr::kSlots);
-                if (!mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
-                               ERR_TIMEOUT_BASE + 11))
+                if (!MLA_TW(11, mbar_wait(&bars->bf_empty[sl], uint32_t(((i / Tr::kSlots) & 1) ^ 1), abort, p.err,
+                               ERR_TIMEOUT_BASE + 11)))
                     break;
                 if (ct == 0) trace_put(p, 3, i * 16 + 2);
                 unsigned char* buf = slots + sl * kSlotBytes;
                 for (int h = 0; h < NK / kStgRows; ++h) {
                     const int64_t k = int64_t(NK / kStgRows) * i + h;
                     const int st = int(k % Tr::kStages);
-                    if (!mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
-                                   ERR_TIMEOUT_BASE + 12)) {
+                    if (!MLA_TW(12, mbar_wait(&bars->full[st], uint32_t((k / Tr::kStages) & 1), abort, p.err,
+                                   ERR_TIMEOUT_BASE + 12))) {
                         okc = false;
                         break;
                     }
+                    MLA_PROF(const long long t_cv = clock64();)
                     const float4* src = reinterpret_cast<const float4*>(stg + st * kStgBytes);
                     float4 a[kU], b[kP];
                     // all loads of the quarter tile first, then the conversions
@@ -629,10 +714,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                     for (int q = 0; q < kU; ++q) a[q] = src[ct + q * kConvThreads];
 #pragma unroll
                     for (int q = 0; q < kP; ++q) b[q] = src[kStgLatBytes / 16 + ct + q * kConvThreads];
-                    // my generic-proxy reads of the staging buffer must be ordered before
-                    // the next TMA (async-proxy) write into it
-                    fence_proxy_async_smem();
-                    mbar_arrive(&bars->stg_empty[st]);
+                    // convert and store into the slot, then release the staging buffer:
+                    // the stores consume every value read from staging, and a warp issues
+                    // in order, so the release cannot issue before all reads returned and
+                    // the next TMA write into the buffer cannot overtake them
 #pragma unroll
                     for (int q = 0; q < kU; ++q) {
                         const int f = ct + q * kConvThreads;          // float4 index in the quarter tile
@@ -649,6 +734,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                                                   (c4 & 1) * 8) =
                             make_uint2(pack_bf16(b[q].x, b[q].y), pack_bf16(b[q].z, b[q].w));
                     }
+                    mbar_arrive(&bars->stg_empty[st]);
+                    MLA_PROF(wacc[15] += clock64() - t_cv;)
                 }
                 if (!okc) break;
                 fence_proxy_async_smem();
@@ -658,6 +745,16 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
         }
     }
 
+#ifdef MLA_TC_PROFILE
+    if (p.prof && lane == 0 && (warp == 0 || warp == 1 || warp == 2 || warp == 4 || warp == 8)) {   // one per role
+        for (int k = 0; k < kProfSlots; ++k)
+            if (wacc[k]) atomicAdd(reinterpret_cast<unsigned long long*>(p.prof + blockIdx.x * kProfSlots + k),
+                                   (unsigned long long)wacc[k]);
+        if (warp == 0)
+            atomicAdd(reinterpret_cast<unsigned long long*>(p.prof + blockIdx.x * kProfSlots + 0),
+                      (unsigned long long)(clock64() - t_kernel0));
+    }
+#endif
     if (threadIdx.x == 0) trace_put(p, 4, 1);
     tc_fence_before();
     __syncthreads();
@@ -863,9 +960,42 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                 cudaHostGetDevicePointer(reinterpret_cast<void**>(&p.trace), trace_host, 0);
             }
         }
+#ifdef MLA_TC_PROFILE
+        long long* prof_dev = nullptr;
+        const size_t prof_bytes = size_t(2 * pl.nclusters) * kProfSlots * sizeof(long long);
+        if (getenv("MLA_TC_PROF") && cudaMalloc(&prof_dev, prof_bytes) == cudaSuccess) {
+            cudaMemsetAsync(prof_dev, 0, prof_bytes, st);
+            p.prof = prof_dev;
+        }
+#endif
         timing_mark(st, true);
         const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p);
         timing_mark(st, false);
+#ifdef MLA_TC_PROFILE
+        if (prof_dev) {
+            static const char* names[kProfSlots] = {
+                "kernel total", "prod stg/slot empty", "prod slot empty(16b)", "mma p_full", "mma q_ready",
+                "mma slot ready", "soft s_full", "soft x_free", "soft x_full", "soft o_done(rescale)",
+                "soft o_done(epilogue)", "conv bf_empty", "conv stage full", "mma s_read", "soft s_full", "conv work", "mma S issue",
+                "mma PV issue", "soft finish work", "exch total", " fin: ld+add", " fin: max+resc",
+                " fin: exp+pack", " fin: P store"};
+            const int64_t nb = 2 * pl.nclusters;
+            long long* h = static_cast<long long*>(malloc(prof_bytes));
+            if (h && cudaMemcpyAsync(h, prof_dev, prof_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                cudaStreamSynchronize(st) == cudaSuccess) {
+                fprintf(stderr, "[mla prof] per-CTA average kcycles over %lld CTAs, %lld tiles per cluster\n",
+                        (long long)nb, (long long)pl.tiles_per_cluster);
+                for (int k = 0; k < kProfSlots; ++k) {
+                    if (!names[k][0]) continue;
+                    double sum = 0;
+                    for (int64_t b = 0; b < nb; ++b) sum += double(h[b * kProfSlots + k]);
+                    fprintf(stderr, "  %-24s %10.1f\n", names[k], sum / nb / 1000.0);
+                }
+            }
+            free(h);
+            cudaFree(prof_dev);
+        }
+#endif
         if (le != cudaSuccess) {
             cudaGetLastError();
             return set_error(MLA_ERR_CUDA, "MLA: launch of the tensor-core attention kernel failed: %s",
