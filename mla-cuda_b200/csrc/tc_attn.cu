@@ -31,11 +31,11 @@
 // storage is converted to bf16 in shared memory after the TMA load, so HBM
 // traffic stays one read of the fp32 cache.
 //
-// Warp roles (256 threads, two warps per SM sub-partition so that each thread
-// may hold up to 255 registers): warp 0 TMA producer, warp 1 MMA issuer and
-// TMEM owner, warps 2-3 fp32->bf16 converters (fp32 storage only), warps 4-7
-// softmax (thread i <-> TMEM lane i <-> head i; a warp reaches only TMEM lanes
-// 32*(warp%4)..+31).
+// Warp roles (640 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
+// owner (warps 2-3 idle), warps 16-19 fp32->bf16 converters (fp32 storage only), warps
+// 4-7 and 12-15 softmax (keys 0-31 / 32-63 of each tile), warps 8-11 exchange
+// (query loads, partial-score push to the peer). Thread i of a warpgroup <->
+// TMEM lane i <-> head i: a warp reaches only TMEM lanes 32*(warp%4)..+31.
 #include "tc.cuh"
 #include "sm100.cuh"
 #include "tc_gemm.cuh"
@@ -65,8 +65,18 @@ constexpr int kRank = 512;
 constexpr int kRope = 64;
 constexpr int kHalf = 256;                  // latent dims per CTA
 constexpr int kRopeHalf = 32;               // rope dims per CTA
-constexpr int kThreads = 512;
-constexpr int kConvThreads = 64;            // fp32 -> bf16 converter threads (warps 2, 3)
+constexpr int kThreads = 640;
+// Registers per thread at launch. The per-warpgroup split below (setmaxnreg)
+// is computed from it, and an increase waits until other warpgroups have
+// released enough, so the host refuses to launch if the compiled kernel does
+// not use exactly this many (a mismatch could leave an increase waiting).
+constexpr int kLaunchRegs = 96;
+// per-thread registers of each warpgroup after the split (see the kernel)
+constexpr int kRegBase = 80, kRegSoftmax = 128, kRegExchange = 72, kRegConvert = 72;
+static_assert(kRegBase + 2 * kRegSoftmax + kRegExchange + kRegConvert <= 5 * kLaunchRegs,
+              "register split exceeds the launch allocation: setmaxnreg.inc would wait forever");
+static_assert(kThreads == 5 * 128, "five warpgroups");
+constexpr int kConvThreads = 128;           // fp32 -> bf16 converter threads (warps 16-19)
 constexpr int kChunkBytes = NK * 128;       // 64 latent dims of a tile: 64 rows of 128 B, 128B swizzle
 constexpr int kRopeChunkBytes = NK * 64;    // 32 rope dims of a tile: 64 rows of 64 B, 64B swizzle
 constexpr int kSlotBytes = 4 * kChunkBytes + kRopeChunkBytes;
@@ -156,7 +166,7 @@ __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
 #define MLA_TW(slot, expr) (expr)
 #define MLA_PROF(stmt)
 #endif
-constexpr int kProfSlots = 24;
+constexpr int kProfSlots = 26;
 
 __device__ __forceinline__ void trace_put(const Params& p, int role, int64_t v) {
     if (p.trace) *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 32 + role) = int(v);
@@ -224,7 +234,7 @@ __device__ __forceinline__ uint32_t swz64(uint32_t r, uint32_t u) { return r * 6
 __device__ __forceinline__ uint32_t swz128(uint32_t r, uint32_t u) { return r * 128u + ((u ^ (r & 7u)) << 4); }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
+__global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tm_ckv, const __grid_constant__ CUtensorMap tm_pe, const Params p)
 {
     using Tr = Traits<T>;
@@ -287,11 +297,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     cluster_sync();   // the peer's barriers exist before any remote arrive
     const uint32_t tmem = bars->tmem_base;
 
-    // Register split per warpgroup (launched with 128 per thread, 512 threads),
-    // set at the top of each role: the exchange warps (warpgroup 2) give 40
-    // back, the softmax warpgroups (1 and 3) take 16 more each; warpgroup 0 (TMA,
-    // MMA, converters) keeps 128. 128 + 144 + 88 + 144 = 504 <= 4 x 128.
+    // Register split per warpgroup, set at the top of each role. setmaxnreg.inc
+    // draws only on registers other warpgroups of this CTA released, so the
+    // per-warp sum over the five warpgroups must stay within 5 x the launch
+    // count (96): the TMA / MMA warpgroup gives 16 back, the exchange and
+    // converter warpgroups 24 each, the softmax warpgroups take 32 more each.
     if (n > 0) {
+        if (warp < 4) setmaxnreg_dec<kRegBase>();
         if (warp == 0 && lane == 0) {
             // ------------------------------------------------------------ TMA producer
             TileIter it = locate(p, t_begin);
@@ -404,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 if (ok && n > 0) issue_pv(n - 1, prev_first);
             }
         } else if (warp >= 8 && warp < 12) {
-            setmaxnreg_dec<88>();
+            setmaxnreg_dec<kRegExchange>();
             // ------------------------------------------------------------ exchange
             // Per tile: loads the next segment's query when one starts (latent slice
             // into TMEM, rope slice into shared memory), waits for my partial scores,
@@ -506,8 +518,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 mbar_arrive(&bars->s_read[sb]);
                 MLA_PROF(wacc[19] += clock64() - t_pr;)
             }
-        } else if ((warp >= 4 && warp < 8) || warp >= 12) {
-            setmaxnreg_inc<144>();
+        } else if ((warp >= 4 && warp < 8) || (warp >= 12 && warp < 16)) {
+            setmaxnreg_inc<kRegSoftmax>();
             // ------------------------------------------------------------ softmax
             // Two warps per TMEM lane quarter: warps 4-7 take keys 0-31 of every
             // tile, warps 12-15 keys 32-63. Per tile each warp adds my partial scores
@@ -639,6 +651,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 }
                 l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
                 MLA_PROF(wacc[22] += clock64() - t_f2; const long long t_f3 = clock64();)
+                // P overwrites my partial scores of tile i: my exchange warps must have
+                // read them first (this warp may be ahead of them, since it needs only
+                // the peer's push)
+                if (!__all_sync(0xffffffffu, MLA_TW(24, mbar_wait(&bars->s_read[sb], uint32_t((i / kSBufs) & 1), abort,
+                                                                  p.err, ERR_TIMEOUT_BASE + 24))))
+                    break;
                 __syncwarp();
                 tmem_st16(tmem + lane_off + kTmemS + sb * NK + hk * 16, pk);
                 tmem_st_wait();
@@ -676,14 +694,15 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
                 }
                 advance(p, it);
             }
-        } else if (warp == 2 || warp == 3) {
+        } else if (warp >= 16) {
+            setmaxnreg_dec<kRegConvert>();
           if constexpr (Tr::kConvert) {
             // ------------------------------------------------------------ fp32 -> bf16
             // Converts four fp32 quarter-tile staging buffers into one bf16 slot.
             // Every thread reads its share of a quarter tile into registers and
             // releases the staging buffer before writing, so the next TMA load can
             // start at once.
-            const int ct = (warp - 2) * 32 + lane;
+            const int ct = (warp - 16) * 32 + lane;
             // Lanes take consecutive 16-byte (4 x fp32) pieces of a staging row, so a
             // warp's shared-memory reads are dense; each piece becomes 8 bytes of bf16.
             constexpr int kU = kStgRows * (kHalf / 4) / kConvThreads;       // latent float4 pieces per thread
@@ -746,7 +765,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_decode_tc_kernel(
     }
 
 #ifdef MLA_TC_PROFILE
-    if (p.prof && lane == 0 && (warp == 0 || warp == 1 || warp == 2 || warp == 4 || warp == 8)) {   // one per role
+    if (p.prof && lane == 0 && (warp == 0 || warp == 1 || warp == 16 || warp == 4 || warp == 8)) {   // one per role
         for (int k = 0; k < kProfSlots; ++k)
             if (wacc[k]) atomicAdd(reinterpret_cast<unsigned long long*>(p.prof + blockIdx.x * kProfSlots + k),
                                    (unsigned long long)wacc[k]);
@@ -938,6 +957,13 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             return set_error(MLA_ERR_CUDA, "MLA: cuTensorMapEncodeTiled failed (alignment of c_kv / pe_cache?)");
 
         auto kern = mla_decode_tc_kernel<T>;
+        cudaFuncAttributes fa{};
+        if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs ||
+            fa.maxThreadsPerBlock < kThreads)
+            return set_error(MLA_ERR_CUDA,
+                             "MLA: decode kernel compiled with %d registers per thread (expected %d; max threads %d): "
+                             "its register split would not fit, not launching", fa.numRegs, kLaunchRegs,
+                             fa.maxThreadsPerBlock);
         const size_t smem = smem_bytes<T>();
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         cudaLaunchConfig_t cfg = {};
@@ -978,7 +1004,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                 "mma slot ready", "soft s_full", "soft x_free", "soft x_full", "soft o_done(rescale)",
                 "soft o_done(epilogue)", "conv bf_empty", "conv stage full", "mma s_read", "soft s_full", "conv work", "mma S issue",
                 "mma PV issue", "soft finish work", "exch total", " fin: ld+add", " fin: max+resc",
-                " fin: exp+pack", " fin: P store"};
+                " fin: exp+pack", " fin: P store", "soft s_read", ""};
             const int64_t nb = 2 * pl.nclusters;
             long long* h = static_cast<long long*>(malloc(prof_bytes));
             if (h && cudaMemcpyAsync(h, prof_dev, prof_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
