@@ -49,6 +49,8 @@
 #include <cstring>
 #include <unistd.h>
 #include <type_traits>
+#include <vector>
+#include <algorithm>
 
 namespace mla {
 
@@ -138,6 +140,7 @@ struct Params {
     int* err;
     int* trace;         // debug only (MLA_TC_TRACE): per-CTA progress words in mapped host memory
     long long* prof;    // debug only (MLA_TC_PROFILE builds): [grid][kProfSlots] cycle counters
+    long long* tl;      // debug only (MLA_TC_TIMELINE builds): [2 CTAs][8 events][kTlTiles] clock64
     int64_t batch, sq, sk;
     int causal;
     float c_log2;       // log2(e) / scale
@@ -167,6 +170,16 @@ __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
 #define MLA_PROF(stmt)
 #endif
 constexpr int kProfSlots = 26;
+// Debug per-tile timeline (compiled in with -DMLA_TC_TIMELINE, printed by the
+// host when MLA_TC_TL is set): clock64 of eight pipeline events for the first
+// kTlTiles tiles of CTAs 0 and 1.
+constexpr int kTlTiles = 256;
+#ifdef MLA_TC_TIMELINE
+#define MLA_TL(ev, i) do { if (p.tl && blockIdx.x < 2 && (i) < kTlTiles) \
+    p.tl[(blockIdx.x * 8 + (ev)) * kTlTiles + (i)] = clock64(); } while (0)
+#else
+#define MLA_TL(ev, i) do { } while (0)
+#endif
 
 __device__ __forceinline__ void trace_put(const Params& p, int role, int64_t v) {
     if (p.trace) *reinterpret_cast<volatile int*>(p.trace + blockIdx.x * 32 + role) = int(v);
@@ -280,7 +293,11 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
         // the softmax warp that consumed the buffer's previous tile)
         for (int i = 0; i < kXBufs; ++i)
             for (int w = 0; w < 4; ++w) {
+#ifdef MLA_EXP_HALFPUSH
+                mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(32 * NK * 2));
+#else
                 mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(32 * NK * 4));
+#endif
                 mbar_arrive_expect_tx(&bars->x_free[i][w], 4u);   // the signal freeing the buffer for tile i+2
             }
         bars->abort = 0;
@@ -361,6 +378,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     if (!MLA_TW(3, mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3)))
                         return false;
                     tc_fence_after();
+                    MLA_TL(6, i);
                     MLA_PROF(const long long t_pv = clock64();)
                     const int sl = int(i % Tr::kSlots);
                     const uint32_t base = smem_slots + sl * kSlotBytes;
@@ -372,6 +390,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                                (first && k == 0) ? 0u : 1u);
                     mma_commit(&bars->bf_empty[sl]);
                     mma_commit(&bars->o_done[sb]);
+                    MLA_TL(1, i);
                     MLA_PROF(wacc[17] += clock64() - t_pv;)
                     return true;
                 };
@@ -407,6 +426,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     for (int k = 0; k < kRopeHalf / 16; ++k)
                         mma_ss(d_s, qd0 + uint64_t((k * 32) >> 4), rd0 + uint64_t((k * 32) >> 4), idesc_s, 1u);
                     mma_commit(&bars->s_full[sb]);
+                    MLA_TL(0, i);
                     MLA_PROF(wacc[16] += clock64() - t_si;)
                     trace_put(p, 1, i * 16 + 2);
                     if (i >= 1) ok = issue_pv(i - 1, prev_first);
@@ -492,6 +512,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 if (!__all_sync(0xffffffffu, MLA_TW(6, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
                                                        ERR_TIMEOUT_BASE + 6))))
                     break;
+                if (warp == 8 && lane == 0) MLA_TL(2, i);
                 tc_fence_after();
                 const int xb = int(i % kXBufs);
                 const int64_t k = i / kXBufs;
@@ -507,8 +528,13 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     uint32_t sr[32];
                     tmem_ld32(tmem + lane_off + kTmemS + sb * NK + h * 32, sr);
                     tmem_ld_wait();
+#ifdef MLA_EXP_HALFPUSH
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+#else
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
+#endif
                         st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + uint32_t(h * 8 + e) * (kHeads * 16),
                                     __uint_as_float(sr[4 * e]), __uint_as_float(sr[4 * e + 1]),
                                     __uint_as_float(sr[4 * e + 2]), __uint_as_float(sr[4 * e + 3]),
@@ -516,6 +542,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 }
                 tc_fence_before();
                 mbar_arrive(&bars->s_read[sb]);
+                if (warp == 8 && lane == 0) MLA_TL(3, i);
                 MLA_PROF(wacc[19] += clock64() - t_pr;)
             }
         } else if ((warp >= 4 && warp < 8) || (warp >= 12 && warp < 16)) {
@@ -562,6 +589,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 if (!__all_sync(0xffffffffu, MLA_TW(8, mbar_wait(&bars->x_full[xb][wq], uint32_t((i / kXBufs) & 1), abort,
                                                                  p.err, ERR_TIMEOUT_BASE + 8, /*cluster_scope=*/true))))
                     break;
+                if (warp == 4 && lane == 0) MLA_TL(4, i);
                 // my partial of my 32 keys (the score buffer is not reused before P.V(i)
                 // is issued) plus the peer's partial
                 MLA_PROF(const long long t_fi = clock64();)
@@ -603,7 +631,11 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 // a maximum that depends on every value it read): announce the bytes of
                 // the buffer's next tile (i+2) and free it for the peer's push.
                 if (hk == 0 && lane == 0) {
-                    if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 4));
+    #ifdef MLA_EXP_HALFPUSH
+                if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 2));
+#else
+                if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 4));
+#endif
                     st_async_b32(sink_peer0 + uint32_t(xb) * 16u, mt, xfree_peer0 + uint32_t(xb) * 32u);
                 }
                 if (first) {
@@ -662,6 +694,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
+                if (warp == 4 && lane == 0) MLA_TL(5, i);
                 MLA_PROF(wacc[23] += clock64() - t_f3;)
                 MLA_PROF(wacc[18] += clock64() - t_fi;)
                 if (lane == 0 && warp == 4) trace_put(p, 2, i * 16 + 4);
@@ -759,6 +792,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 if (!okc) break;
                 fence_proxy_async_smem();
                 mbar_arrive(&bars->bf_full[sl]);
+                if (warp == 16 && lane == 0) MLA_TL(7, i);
             }
           }
         }
@@ -994,9 +1028,50 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             p.prof = prof_dev;
         }
 #endif
+#ifdef MLA_TC_TIMELINE
+        long long* tl_dev = nullptr;
+        const size_t tl_bytes = size_t(2) * 8 * kTlTiles * sizeof(long long);
+        if (getenv("MLA_TC_TL") && cudaMalloc(&tl_dev, tl_bytes) == cudaSuccess) {
+            cudaMemsetAsync(tl_dev, 0, tl_bytes, st);
+            p.tl = tl_dev;
+        }
+#endif
         timing_mark(st, true);
         const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, tm_ckv, tm_pe, p);
         timing_mark(st, false);
+#ifdef MLA_TC_TIMELINE
+        if (tl_dev) {
+            std::vector<long long> h(size_t(2) * 8 * kTlTiles);
+            if (cudaMemcpyAsync(h.data(), tl_dev, tl_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                cudaStreamSynchronize(st) == cudaSuccess) {
+                const int64_t nt = std::min<int64_t>(pl.tiles_per_cluster, kTlTiles);
+                for (int c = 0; c < 2; ++c) {
+                    auto at = [&](int ev, int64_t i) { return double(h[(c * 8 + ev) * kTlTiles + i]); };
+                    double d[10] = {0};
+                    int cnt = 0;
+                    for (int64_t i = 8; i + 3 < nt - 4; ++i, ++cnt) {
+                        d[0] += at(5, i + 1) - at(5, i);        // tile period (softmax p_full)
+                        d[1] += at(5, i) - at(4, i);            // softmax: x_full seen -> p_full
+                        d[2] += at(6, i) - at(5, i);            // p_full -> MMA sees it
+                        d[3] += at(1, i) - at(6, i);            // PV issue
+                        d[4] += at(0, i + 2) - at(1, i);        // PV(i) issued -> S(i+2) issued
+                        d[5] += at(2, i + 2) - at(0, i + 2);    // S(i+2) issued -> exchange sees s_full
+                        d[6] += at(3, i + 2) - at(2, i + 2);    // exchange push
+                        d[7] += at(4, i + 2) - at(3, i + 2);    // my push done -> softmax sees peer's push
+                        d[8] += at(0, i + 2) - at(7, i + 2);    // slot ready -> S issued
+                        d[9] += at(4, i) - at(5, i - 1);        // softmax idle between tiles
+                    }
+                    static const char* nm[10] = {"tile period", "softmax x_full->p_full", "p_full->MMA sees",
+                                                 "PV issue", "PV(i)->S(i+2) issued", "S issued->exch s_full",
+                                                 "exch push", "push->peer data seen", "slot ready->S issued",
+                                                 "softmax idle between tiles"};
+                    fprintf(stderr, "[mla timeline] CTA %d, %d tiles: average cycles\n", c, cnt);
+                    for (int k = 0; k < 10; ++k) fprintf(stderr, "  %-28s %9.0f\n", nm[k], cnt ? d[k] / cnt : 0.0);
+                }
+            }
+            cudaFree(tl_dev);
+        }
+#endif
 #ifdef MLA_TC_PROFILE
         if (prof_dev) {
             static const char* names[kProfSlots] = {
