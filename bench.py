@@ -57,6 +57,9 @@ def parse():
     ap.add_argument("--no-graph", action="store_true",
                     help="launch the timed layer forwards one by one instead of replaying a CUDA graph of one")
     ap.add_argument("--no-parity", action="store_true", help="skip the sampled-sequence parity check")
+    ap.add_argument("--weights", default="packed", choices=["packed", "plain"],
+                    help="tensor precision, fp32 storage: Q-prep from weights packed once to bf16 (default) or "
+                         "from the fp32 weights on every call")
     ap.add_argument("--no-key-shard-c2", action="store_true",
                     help="with --gpus N > 1, skip the extra key-sharded c2 measurement")
     ap.add_argument("--qprep", default="redundant", choices=["heads", "redundant"],
@@ -166,6 +169,7 @@ class ClockSampler:
 
 
 KEY_SHARDED = {"on": False, "heads": False}
+PACKED = {"w": None}   # PackedQWeights when the step uses pre-packed Q-prep weights
 
 # DRAM bytes per launch of the decode kernel, from the ncu capture named below
 # (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (config, precision,
@@ -181,6 +185,8 @@ def run_forward(mcc, t, w, precision):
         from mla_custom_cuda import sharding
         qa, qr = sharding.head_sharded_q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
                                                   t["positions"], w.nope, w.rope, mc.EPS, precision=precision)
+    elif PACKED["w"] is not None and precision == "tensor":
+        qa, qr = mcc.q_absorbed_packed(t["x"], PACKED["w"], t["q_norm_w"], t["positions"], mc.EPS)
     else:
         qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
                                    w.nope, w.rope, mc.EPS, precision=precision)
@@ -280,10 +286,7 @@ def parity_sample(mcc, t, w, precision, seqs):
     """rel-L2 of the GPU layer output against the fp64 oracle, and the
     argmax-of-scores agreement, on a few sequences of the benched inputs."""
     from oracle import mla_oracle as orc
-    qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
-                               w.nope, w.rope, mc.EPS, precision=precision)
-    out = mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, causal=w.causal,
-                               precision=precision)
+    out, qa, qr = run_forward(mcc, t, w, precision)   # the benched path
     torch.cuda.synchronize()
     W = {k: t[k].double().cpu() for k in ("W_q_a", "q_norm_w", "W_q_b", "W_uk", "W_uv")}
     errs, errs32, noise, agree = [], [], [], []
@@ -387,6 +390,11 @@ def main_ours(args):
     else:
         t = mc.make_inputs(w, device=dev, gen="device", seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
+    if (args.weights == "packed" and precision == "tensor" and w.dtype == torch.float32
+            and not KEY_SHARDED["heads"]):
+        # weight-load time, outside every timed region: one bf16 copy of W_q_a, W_q_b, W_uk
+        PACKED["w"] = mcc.pack_q_weights(t["W_q_a"], t["W_q_b"], t["W_uk"], w.nope, w.rope)
+        torch.cuda.synchronize()
 
     def barrier():
         if world > 1:
@@ -487,10 +495,13 @@ def main_ours(args):
         fwd = att + qp if prec != precision else ms
         stages[prec] = {"q_absorbed_ms": qp, "mla_attention_ms": att, "layer_ms": fwd,
                         "tokens_per_s": tokens_total / (fwd * 1e-3)}
+        if prec == "tensor" and PACKED["w"] is not None:
+            stages[prec]["q_absorbed_packed_ms"] = max_over_ranks(device_timed(stream, lambda: mcc.q_absorbed_packed(
+                t["x"], PACKED["w"], t["q_norm_w"], t["positions"], mc.EPS), n_att), world, dev)
         if prec == "tensor" and kernel_ms:
             stages[prec]["decode_kernel_ms"] = kernel_ms
     att_ms = stages[precision]["mla_attention_ms"]
-    q_ms = stages[precision]["q_absorbed_ms"]
+    q_ms = stages[precision].get("q_absorbed_packed_ms", stages[precision]["q_absorbed_ms"])
 
     cache_b, weight_b, act_b = workload_bytes(w, B, sk_local)
     qf, af = workload_flops(w, B)
@@ -560,8 +571,10 @@ def main_ours(args):
             "data": "synthetic (seeded N(0,1) cache / activations, N(0,0.02) weights)",
             "config": line_config(w, world, shard),
             "precision": precision,
-            "launch": ("CUDA graph of one layer forward (q_absorbed_ex + mla_attention_ex), replayed per step"
+            "launch": ("CUDA graph of one layer forward (q_absorbed + mla_attention), replayed per step"
                        if use_graph else "eager calls per step")
+                      + ("; Q-prep from weights packed once to bf16 at load (q_absorbed_packed)"
+                         if PACKED["w"] is not None else "")
                       + (", Q-prep head-sharded + all-gather of q" if KEY_SHARDED["heads"] else ""),
             "stages": stages,
             "roofline": {"bound": "hbm",

@@ -116,6 +116,37 @@ MLA_API mla_status_t mla_q_absorbed(
     void* q_absorbed, void* q_rope,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------- pre-packed Q weights --
+ * Beside the drop-in (the reference converts nothing; its callers pass the
+ * fp32 weights, made contiguous, on every call: exhaustive_benchmark_suite.py:
+ * 261-265, stage_profile.py:57-63). For fp32 storage in tensor precision, the
+ * Q-prep weights W_q_a, W_q_b and W_uk can be converted once, at weight-load
+ * time, to one bf16 buffer of mla_pack_q_weights_size() bytes; then
+ * mla_q_absorbed_packed computes q_absorbed / q_rope from it, streaming half the
+ * weight bytes of mla_q_absorbed with MLA_PREC_TENSOR (bf16 operands, fp32
+ * accumulation, fp32 RMSNorm and RoPE; rel-L2 <= 2e-2). x, q_norm_w, positions
+ * and the outputs are as for mla_q_absorbed (fp32). The packed buffer stays
+ * valid as long as the weights do not change.
+ */
+MLA_API mla_status_t mla_pack_q_weights_size(
+    mla_dtype_t dtype, int64_t hidden, int64_t q_lora, int64_t heads,
+    int64_t nope, int64_t rope, int64_t kv_rank, size_t* bytes);
+
+MLA_API mla_status_t mla_pack_q_weights(
+    mla_dtype_t dtype, const void* W_q_a, const void* W_q_b, const void* W_uk,
+    int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank,
+    void* packed, size_t packed_bytes, void* stream);
+
+MLA_API mla_status_t mla_q_absorbed_packed_workspace_size(
+    mla_dtype_t dtype, int64_t batch, int64_t sq, int64_t hidden, int64_t q_lora,
+    int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank, size_t* bytes);
+
+MLA_API mla_status_t mla_q_absorbed_packed(
+    mla_dtype_t dtype, const void* x, const void* packed, const void* q_norm_w,
+    const int64_t* positions, int64_t batch, int64_t sq, int64_t hidden, int64_t q_lora,
+    int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank, double eps,
+    void* q_absorbed, void* q_rope, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------- attention --
  * Replaces launch_mla_attention (mla_kernels.cu:1479-1682): scores
  * (q_absorbed . c_kv + q_rope . pe_cache) / scale, softmax over the keys,

@@ -164,6 +164,66 @@ mla_status_t mla_q_absorbed(mla_dtype_t dtype, mla_precision_t precision, const 
     return dispatch(dtype, [&](auto t) { return qprep_exact<decltype(t)>(a, st); });
 }
 
+mla_status_t mla_pack_q_weights_size(mla_dtype_t dtype, int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope,
+                                    int64_t rope, int64_t kv_rank, size_t* bytes) {
+    MLA_TRY(validate_q(dtype, MLA_PREC_TENSOR, 1, 1, hidden, q_lora, heads, nope, rope, kv_rank));
+    if (dtype != MLA_DTYPE_F32)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: weight packing is for fp32 storage (16-bit weights are used as is)");
+    if (!bytes) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA: bytes must not be NULL");
+    *bytes = pack_q_weights_bytes(hidden, q_lora, heads, nope, rope, kv_rank);
+    return MLA_OK;
+}
+
+mla_status_t mla_pack_q_weights(mla_dtype_t dtype, const void* W_q_a, const void* W_q_b, const void* W_uk,
+                                int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope, int64_t rope,
+                                int64_t kv_rank, void* packed, size_t packed_bytes, void* stream) {
+    size_t need = 0;
+    MLA_TRY(mla_pack_q_weights_size(dtype, hidden, q_lora, heads, nope, rope, kv_rank, &need));
+    if (!W_q_a || !W_q_b || !W_uk || !packed)
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA pack_q_weights: null pointer");
+    if (packed_bytes < need)
+        return set_error(MLA_ERR_WORKSPACE, "MLA pack_q_weights: %zu bytes needed, %zu given", need, packed_bytes);
+    if (hidden * q_lora % 4 != 0 || q_lora * heads * (nope + rope) % 4 != 0 || heads * nope * kv_rank % 4 != 0)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA pack_q_weights: weight sizes must be multiples of 4");
+    return pack_q_weights(static_cast<const float*>(W_q_a), static_cast<const float*>(W_q_b),
+                          static_cast<const float*>(W_uk), hidden, q_lora, heads, nope, rope, kv_rank, packed,
+                          static_cast<cudaStream_t>(stream));
+}
+
+mla_status_t mla_q_absorbed_packed_workspace_size(mla_dtype_t dtype, int64_t batch, int64_t sq, int64_t hidden,
+                                                  int64_t q_lora, int64_t heads, int64_t nope, int64_t rope,
+                                                  int64_t kv_rank, size_t* bytes) {
+    MLA_TRY(validate_q(dtype, MLA_PREC_TENSOR, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank));
+    if (dtype != MLA_DTYPE_F32) return set_error(MLA_ERR_UNSUPPORTED, "MLA: packed Q-prep is for fp32 storage");
+    if (!bytes) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA: bytes must not be NULL");
+    QArgs a{};
+    a.batch = batch; a.sq = sq; a.hidden = hidden; a.q_lora = q_lora;
+    a.heads = heads; a.nope = nope; a.rope = rope; a.kv_rank = kv_rank;
+    *bytes = (batch * sq == 0) ? 0 : qprep_packed_workspace(a);
+    return MLA_OK;
+}
+
+mla_status_t mla_q_absorbed_packed(mla_dtype_t dtype, const void* x, const void* packed, const void* q_norm_w,
+                                   const int64_t* positions, int64_t batch, int64_t sq, int64_t hidden,
+                                   int64_t q_lora, int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank,
+                                   double eps, void* q_absorbed, void* q_rope, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    size_t need = 0;
+    MLA_TRY(mla_q_absorbed_packed_workspace_size(dtype, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank, &need));
+    if (batch * sq == 0) return MLA_OK;
+    if (!x || !packed || !q_norm_w || !positions || !q_absorbed || !q_rope)
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA q_absorbed_packed: null operand pointer");
+    QArgs a{x, nullptr, q_norm_w, nullptr, nullptr, positions, batch, sq, hidden, q_lora, heads, nope, rope, kv_rank,
+            eps, q_absorbed, q_rope, workspace, workspace_bytes};
+    if (!qprep_packed_supported(a))
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA q_absorbed_packed: shape not covered (needs q_lora, heads*(nope+rope), "
+                                              "kv_rank multiples of 32, hidden and nope multiples of 8, q_lora <= 4096)");
+    if (!workspace || workspace_bytes < need)
+        return set_error(MLA_ERR_WORKSPACE, "MLA q_absorbed_packed: workspace of %zu bytes needed, %zu given", need,
+                         workspace ? workspace_bytes : size_t(0));
+    return qprep_packed(a, packed, static_cast<cudaStream_t>(stream));
+}
+
 mla_status_t mla_attention_workspace_size(mla_dtype_t dtype, mla_precision_t precision, int64_t batch, int64_t sq,
                                           int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim,
                                           int causal, size_t* bytes) {

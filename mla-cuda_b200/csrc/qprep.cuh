@@ -34,6 +34,14 @@ template <typename T> bool qprep_tensor_supported(const QArgs& a);
 template <typename T> size_t qprep_tensor_workspace(const QArgs& a);
 template <typename T> mla_status_t qprep_tensor(const QArgs& a, cudaStream_t st);
 
+// fp32 storage, tensor precision, with bf16 weights packed once (qprep_exact.cu)
+bool qprep_packed_supported(const QArgs& a);
+size_t pack_q_weights_bytes(int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank);
+mla_status_t pack_q_weights(const float* W_q_a, const float* W_q_b, const float* W_uk, int64_t hidden, int64_t q_lora,
+                            int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank, void* packed, cudaStream_t st);
+size_t qprep_packed_workspace(const QArgs& a);
+mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st);
+
 template <typename T> size_t attn_exact_workspace(const AArgs& a);
 template <typename T> mla_status_t attn_exact(const AArgs& a, cudaStream_t st);
 

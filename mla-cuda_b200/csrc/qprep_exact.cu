@@ -183,10 +183,10 @@ __global__ void __launch_bounds__(256) rope_gather_kernel(
 // Vectorised 2a-norm for an fp32 accumulator: one block of 256 threads per row,
 // each thread owning up to kVec float4 pieces of the row, all split-K partial loads
 // of a piece issued together. Same sums, in the same order, as lat_norm_kernel.
-template <typename T>
+template <typename T, typename OutT = T>
 __global__ void __launch_bounds__(1024) lat_norm_vec_kernel(
     const float* __restrict__ P1, int splits, const T* __restrict__ gain,
-    T* __restrict__ q_lat, int64_t M, int64_t q_lora, float eps)
+    OutT* __restrict__ q_lat, int64_t M, int64_t q_lora, float eps)
 {
     constexpr int kMaxSplits = 16;                 // all split loads of a piece in flight at once
     const int64_t m = blockIdx.x;
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(1024) lat_norm_vec_kernel(
         const float f[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-            q_lat[m * q_lora + 4 * c + k] = cvt<T>(f[k] * inv_rms * cvt<float>(gain[4 * c + k]));
+            q_lat[m * q_lora + 4 * c + k] = cvt<OutT>(f[k] * inv_rms * cvt<float>(gain[4 * c + k]));
     }
 }
 
@@ -626,6 +626,162 @@ mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3) {
     g3.C = a.q_absorbed; g3.c_is_t = true; g3.c_ldm = a.heads * a.kv_rank; g3.c_ldz = a.kv_rank;
     g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err; g3.split3 = split3;
     return tc_gemm<T>(g3, st);
+}
+
+// ------------------------------------------------------- pre-packed weights
+// fp32 storage, MLA_PREC_TENSOR: the three Q-prep weights are converted once to
+// bf16 (mla_pack_q_weights) and the projections run as kind::f16 tcgen05 GEMMs
+// on them, so each call streams half the weight bytes of the kind::tf32 path.
+// x is cast to bf16 per call (its 128 x 7168 values are small next to the
+// weights); split-K partials, the RMSNorm and the RoPE stay fp32; q_lat and
+// q_nope, the left operands of 2a2 and 2c, are bf16; q_absorbed and q_rope are
+// written in fp32.
+namespace {
+
+__global__ void __launch_bounds__(256) cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
+                                                        int64_t n4) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
+        __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+        uint2 o;
+        o.x = *reinterpret_cast<uint32_t*>(&lo);
+        o.y = *reinterpret_cast<uint32_t*>(&hi);
+        reinterpret_cast<uint2*>(dst)[i] = o;
+    }
+}
+
+mla_status_t cast_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t st) {
+    const int64_t n4 = n / 4;
+    int64_t blocks = ceil_div(n4, 256);
+    if (blocks > 8LL * sm_count()) blocks = 8LL * sm_count();
+    if (blocks < 1) blocks = 1;
+    cast_bf16_kernel<<<unsigned(blocks), 256, 0, st>>>(src, dst, n4);
+    return check_launch("bf16 cast");
+}
+
+struct PackLayout {
+    size_t off_qa, off_qb, off_uk, total;
+};
+
+PackLayout pack_layout(int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank) {
+    PackLayout l{};
+    size_t off = 0;
+    l.off_qa = off; off = align_up(off + size_t(hidden) * q_lora * 2, 256);
+    l.off_qb = off; off = align_up(off + size_t(q_lora) * heads * (nope + rope) * 2, 256);
+    l.off_uk = off; off = align_up(off + size_t(heads) * nope * kv_rank * 2, 256);
+    l.total = off;
+    return l;
+}
+
+struct QPPlan {
+    int split1, split2;
+    int64_t chunk1, chunk2;
+    size_t off_x, off_p1, off_qlat, off_p2, off_qnope, total;
+};
+
+QPPlan make_pplan(const QArgs& a) {
+    using B16 = __nv_bfloat16;
+    QPPlan p{};
+    const int64_t M = a.batch * a.sq;
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    const int64_t bk = tc_gemm_bk<B16>();
+    const int64_t mt = ceil_div(M, 128);
+    p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), M, a.hidden, bk, p.chunk1);
+    p.split2 = tc_split(mt * ceil_div(ncols, 128), M, a.q_lora, bk, p.chunk2);
+    size_t off = 0;
+    p.off_x = off;     off = align_up(off + size_t(M) * a.hidden * sizeof(B16), 256);
+    p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(float), 256);
+    p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(B16), 256);
+    p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(float), 256);
+    p.off_qnope = off; off = align_up(off + size_t(M) * a.heads * a.nope * sizeof(B16), 256);
+    p.total = off;
+    return p;
+}
+
+}  // namespace
+
+bool qprep_packed_supported(const QArgs& a) {
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    return a.q_lora % 32 == 0 && ncols % 32 == 0 && a.kv_rank % 32 == 0 && a.hidden % 8 == 0 && a.q_lora % 8 == 0 &&
+           a.nope % 8 == 0 && a.rope % 4 == 0 && a.nope % 4 == 0 && a.q_lora <= 4096 && a.batch * a.sq > 0 &&
+           (a.batch * a.sq * a.hidden) % 4 == 0;
+}
+
+size_t pack_q_weights_bytes(int64_t hidden, int64_t q_lora, int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank) {
+    return pack_layout(hidden, q_lora, heads, nope, rope, kv_rank).total;
+}
+
+mla_status_t pack_q_weights(const float* W_q_a, const float* W_q_b, const float* W_uk, int64_t hidden, int64_t q_lora,
+                            int64_t heads, int64_t nope, int64_t rope, int64_t kv_rank, void* packed,
+                            cudaStream_t st) {
+    const PackLayout l = pack_layout(hidden, q_lora, heads, nope, rope, kv_rank);
+    char* base = static_cast<char*>(packed);
+    MLA_TRY(cast_bf16(W_q_a, reinterpret_cast<__nv_bfloat16*>(base + l.off_qa), hidden * q_lora, st));
+    MLA_TRY(cast_bf16(W_q_b, reinterpret_cast<__nv_bfloat16*>(base + l.off_qb), q_lora * heads * (nope + rope), st));
+    return cast_bf16(W_uk, reinterpret_cast<__nv_bfloat16*>(base + l.off_uk), heads * nope * kv_rank, st);
+}
+
+size_t qprep_packed_workspace(const QArgs& a) { return make_pplan(a).total; }
+
+mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st) {
+    using B16 = __nv_bfloat16;
+    const QPPlan p = make_pplan(a);
+    const PackLayout l = pack_layout(a.hidden, a.q_lora, a.heads, a.nope, a.rope, a.kv_rank);
+    const char* pk = static_cast<const char*>(packed);
+    const int64_t M = a.batch * a.sq;
+    const int64_t ncols = a.heads * (a.nope + a.rope);
+    char* ws = static_cast<char*>(a.workspace);
+    DeviceStatus* dst = nullptr;
+    MLA_TRY(device_status_block(&dst));
+    int* err = &dst->code;
+    B16* x16 = reinterpret_cast<B16*>(ws + p.off_x);
+    float* P1 = reinterpret_cast<float*>(ws + p.off_p1);
+    B16* q_lat = reinterpret_cast<B16*>(ws + p.off_qlat);
+    float* P2 = reinterpret_cast<float*>(ws + p.off_p2);
+    B16* q_nope = reinterpret_cast<B16*>(ws + p.off_qnope);
+    MLA_TRY(cast_bf16(static_cast<const float*>(a.x), x16, M * a.hidden, st));
+
+    TcGemm g1{};   // 2a1: x [M, hidden] @ W_q_a [hidden, q_lora], bf16 operands, fp32 partials
+    g1.A = x16; g1.a_dims[0] = a.hidden; g1.a_dims[1] = 1; g1.a_dims[2] = M; g1.a_ld[0] = a.hidden; g1.a_ld[1] = a.hidden;
+    g1.B = pk + l.off_qa; g1.b_mn = true; g1.b_dims[0] = a.q_lora; g1.b_dims[1] = a.hidden; g1.b_dims[2] = 1;
+    g1.b_ld[0] = a.q_lora; g1.b_ld[1] = a.q_lora * a.hidden;
+    g1.M = M; g1.N = a.q_lora; g1.K = a.hidden; g1.Z = p.split1; g1.spb = p.split1; g1.k_chunk = p.chunk1;
+    g1.C = P1; g1.c_is_t = false; g1.c_ldm = a.q_lora; g1.c_ldz = M * a.q_lora; g1.bn = 128; g1.err = err;
+    MLA_TRY(tc_gemm<B16>(g1, st));
+
+    {   // 2a-norm: fp32 arithmetic, bf16 latent for 2a2
+        const unsigned threads = unsigned((a.q_lora / 4 + 31) / 32 * 32);
+        if (p.split1 > 16) return set_error(MLA_ERR_UNSUPPORTED, "MLA: packed Q-prep split-K above 16");
+        lat_norm_vec_kernel<float, B16><<<unsigned(M), threads, 0, st>>>(
+            P1, p.split1, static_cast<const float*>(a.q_norm_w), q_lat, M, a.q_lora, float(a.eps));
+        MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
+    }
+
+    TcGemm g2{};   // 2a2: q_lat [M, q_lora] @ W_q_b [q_lora, H*(nope+rope)]
+    g2.A = q_lat; g2.a_dims[0] = a.q_lora; g2.a_dims[1] = 1; g2.a_dims[2] = M; g2.a_ld[0] = a.q_lora; g2.a_ld[1] = a.q_lora;
+    g2.B = pk + l.off_qb; g2.b_mn = true; g2.b_dims[0] = ncols; g2.b_dims[1] = a.q_lora; g2.b_dims[2] = 1;
+    g2.b_ld[0] = ncols; g2.b_ld[1] = ncols * a.q_lora;
+    g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = p.split2; g2.spb = p.split2; g2.k_chunk = p.chunk2;
+    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err;
+    MLA_TRY(tc_gemm<B16>(g2, st));
+
+    RopeTable<float> tab{};
+    for (int64_t j = 0; j < a.rope / 2; ++j) {
+        const double pw = std::pow(10000.0, double(2 * j) / double(a.rope));
+        tab.inv_freq[j] = 1.0f / float(pw);
+    }
+    MLA_TRY((launch_rope_gather<float, B16>(P2, p.split2, a.positions, q_nope, static_cast<float*>(a.q_rope), M, a.sq,
+                                            a.heads, a.nope, a.rope, tab, nullptr, st)));
+
+    TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h], fp32 output
+    g3.A = q_nope; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;
+    g3.a_ld[0] = a.nope; g3.a_ld[1] = a.heads * a.nope;
+    g3.B = pk + l.off_uk; g3.b_mn = true; g3.b_dims[0] = a.kv_rank; g3.b_dims[1] = a.nope; g3.b_dims[2] = a.heads;
+    g3.b_ld[0] = a.kv_rank; g3.b_ld[1] = a.nope * a.kv_rank;
+    g3.M = M; g3.N = a.kv_rank; g3.K = a.nope; g3.Z = int(a.heads); g3.spb = 1; g3.k_chunk = a.nope;
+    g3.C = a.q_absorbed; g3.c_is_t = false; g3.c_ldm = a.heads * a.kv_rank; g3.c_ldz = a.kv_rank;
+    g3.bn = a.kv_rank % 256 == 0 ? 256 : 128; g3.err = err;
+    return tc_gemm<B16>(g3, st);
 }
 
 #define MLA_QT(T) \

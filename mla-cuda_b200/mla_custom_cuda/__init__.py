@@ -39,7 +39,7 @@ __all__ = [
     "mla_attention_partial", "lse_combine",
     "set_precision", "get_precision", "library_path", "abi_version",
     "device_status", "clear_device_status", "check_device", "set_wait_limit_ns", "wait_selftest",
-    "kernel_timing",
+    "kernel_timing", "pack_q_weights", "q_absorbed_packed", "PackedQWeights",
 ]
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmla_b200.so"
@@ -87,6 +87,15 @@ def _load() -> ctypes.CDLL:
     lib.mla_set_wait_limit_ns.argtypes = [ctypes.c_uint64, _c_vp]
     lib.mla_wait_selftest.restype = ctypes.c_int
     lib.mla_wait_selftest.argtypes = [_c_vp]
+    lib.mla_pack_q_weights_size.restype = ctypes.c_int
+    lib.mla_pack_q_weights_size.argtypes = [ctypes.c_int] + [_c_i64] * 6 + [ctypes.POINTER(_c_size)]
+    lib.mla_pack_q_weights.restype = ctypes.c_int
+    lib.mla_pack_q_weights.argtypes = [ctypes.c_int] + [_c_vp] * 3 + [_c_i64] * 6 + [_c_vp, _c_size, _c_vp]
+    lib.mla_q_absorbed_packed_workspace_size.restype = ctypes.c_int
+    lib.mla_q_absorbed_packed_workspace_size.argtypes = [ctypes.c_int] + [_c_i64] * 8 + [ctypes.POINTER(_c_size)]
+    lib.mla_q_absorbed_packed.restype = ctypes.c_int
+    lib.mla_q_absorbed_packed.argtypes = ([ctypes.c_int] + [_c_vp] * 4 + [_c_i64] * 8
+                                          + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
     lib.mla_timing_enable.restype = ctypes.c_int
     lib.mla_timing_enable.argtypes = [ctypes.c_int]
     lib.mla_timing_read.restype = ctypes.c_int
@@ -265,6 +274,73 @@ def q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim: int, rop
                                  rope_dim, R, float(eps), qa.data_ptr(), qr.data_ptr(), ws.data_ptr(),
                                  ws.numel(), stream)
     _raise_status(st, "q_absorbed")
+    _after_call(device)
+    return [qa, qr]
+
+
+class PackedQWeights:
+    """W_q_a, W_q_b and W_uk converted once to bf16 (one device buffer), for
+    q_absorbed_packed. Holds the dimensions it was packed with."""
+
+    def __init__(self, buf: torch.Tensor, hidden: int, q_lora: int, heads: int, nope: int, rope: int,
+                 kv_rank: int):
+        self.buf, self.hidden, self.q_lora = buf, hidden, q_lora
+        self.heads, self.nope, self.rope, self.kv_rank = heads, nope, rope, kv_rank
+
+    @property
+    def device(self):
+        return self.buf.device
+
+
+def pack_q_weights(W_q_a, W_q_b, W_uk, nope_dim: int, rope_dim: int) -> PackedQWeights:
+    """One-time bf16 packing of the fp32 Q-prep weights (at weight-load time).
+    The reference has no such step: its callers pass the fp32 weights on every
+    call (exhaustive_benchmark_suite.py:261-265)."""
+    dtype, device = _float_operands([("W_q_a", W_q_a), ("W_q_b", W_q_b), ("W_uk", W_uk)])
+    _check(dtype == torch.float32, "pack_q_weights: fp32 weights only (16-bit weights are used as they are)")
+    _check(W_q_a.dim() == 2 and W_q_b.dim() == 2 and W_uk.dim() == 3, "pack_q_weights: bad weight ranks")
+    hidden, q_lora = W_q_a.shape
+    H, nope_w, R = W_uk.shape
+    nope_dim, rope_dim = int(nope_dim), int(rope_dim)
+    _check(nope_w == nope_dim and tuple(W_q_b.shape) == (q_lora, H * (nope_dim + rope_dim)),
+           "pack_q_weights: inconsistent weight shapes")
+    nbytes = _c_size(0)
+    _raise_status(_lib.mla_pack_q_weights_size(0, hidden, q_lora, H, nope_dim, rope_dim, R, ctypes.byref(nbytes)),
+                  "pack_q_weights")
+    buf = torch.empty(int(nbytes.value), dtype=torch.uint8, device=device)
+    Wa, Wb, Wk = (t.contiguous() for t in (W_q_a, W_q_b, W_uk))
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_pack_q_weights(0, Wa.data_ptr(), Wb.data_ptr(), Wk.data_ptr(), hidden, q_lora, H,
+                                              nope_dim, rope_dim, R, buf.data_ptr(), buf.numel(),
+                                              _stream_of(device)), "pack_q_weights")
+    return PackedQWeights(buf, hidden, q_lora, H, nope_dim, rope_dim, R)
+
+
+def q_absorbed_packed(x, packed: PackedQWeights, q_norm_w, positions, eps: float) -> List[torch.Tensor]:
+    """q_absorbed (tensor precision, fp32 storage) from weights packed by
+    pack_q_weights: returns [q_absorbed [B,Sq,H,kv_rank], q_rope [B,Sq,H,rope]] in fp32."""
+    dtype, device = _float_operands([("x", x), ("q_norm_w", q_norm_w)])
+    _check(dtype == torch.float32, "q_absorbed_packed: fp32 x and q_norm_w")
+    _check(isinstance(packed, PackedQWeights) and packed.device == device, "packed must be a PackedQWeights on x's device")
+    _check(x.dim() == 3 and x.shape[2] == packed.hidden, f"x must be [B, Sq, {packed.hidden}]")
+    _check(q_norm_w.dim() == 1 and q_norm_w.shape[0] == packed.q_lora, "q_norm_w must be [q_lora]")
+    B, Sq, _ = x.shape
+    _check(isinstance(positions, torch.Tensor) and positions.dim() == 1 and positions.shape[0] == Sq,
+           "positions must be a 1-D tensor of length Sq")
+    xc, g = x.contiguous(), q_norm_w.contiguous()
+    pos = positions.to(device=device, dtype=torch.int64).contiguous()
+    H, R, D = packed.heads, packed.kv_rank, packed.rope
+    qa = torch.empty((B, Sq, H, R), dtype=dtype, device=device)
+    qr = torch.empty((B, Sq, H, D), dtype=dtype, device=device)
+    nbytes = _c_size(0)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_q_absorbed_packed_workspace_size(0, B, Sq, packed.hidden, packed.q_lora, H, packed.nope,
+                                                                D, R, ctypes.byref(nbytes)), "q_absorbed_packed")
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=device)
+        st = _lib.mla_q_absorbed_packed(0, xc.data_ptr(), packed.buf.data_ptr(), g.data_ptr(), pos.data_ptr(), B, Sq,
+                                        packed.hidden, packed.q_lora, H, packed.nope, D, R, float(eps),
+                                        qa.data_ptr(), qr.data_ptr(), ws.data_ptr(), ws.numel(), _stream_of(device))
+    _raise_status(st, "q_absorbed_packed")
     _after_call(device)
     return [qa, qr]
 

@@ -162,3 +162,22 @@ def test_key_shards_partial_and_combine(mcc, precision, parts):
     assert rel_l2(merged, full) < tol
     _, ref_lse = orc.mla_attention_partial(*(t.double().cpu() for t in (qa, qr, ck, pe, wuv)), mc.SCALE)
     assert rel_l2(L.cpu(), ref_lse) < (1e-6 if precision == "exact" else 1e-3)
+
+
+@pytest.mark.parametrize("B,Sq", [(1, 1), (5, 3), (128, 1), (200, 1)])
+def test_packed_q_absorbed_vs_oracle(mcc, B, Sq):
+    """Q-prep from bf16-packed weights (fp32 storage, tensor precision) against the
+    fp64 oracle, and against the unpacked tensor-precision path."""
+    w = mc.Workload("q", B, Sq, 8)
+    t = mc.make_inputs(w, seed=B * 7 + Sq)
+    g = {k: v.to(DEV) for k, v in t.items()}
+    packed = mcc.pack_q_weights(g["W_q_a"], g["W_q_b"], g["W_uk"], mc.NOPE, mc.ROPE)
+    qa, qr = mcc.q_absorbed_packed(g["x"], packed, g["q_norm_w"], g["positions"], mc.EPS)
+    assert qa.dtype == torch.float32 and qa.shape == (B, Sq, 128, 512) and qr.shape == (B, Sq, 128, 64)
+    t64 = {k: (v.double() if v.is_floating_point() else v) for k, v in t.items()}
+    ra, rr = orc.q_absorbed(t64["x"], t64["W_q_a"], t64["q_norm_w"], t64["W_q_b"], t64["W_uk"], t64["positions"])
+    assert rel_l2(qa.cpu(), ra) < TOL
+    assert rel_l2(qr.cpu(), rr) < TOL
+    qa2, qr2 = mcc.q_absorbed_ex(g["x"], g["W_q_a"], g["q_norm_w"], g["W_q_b"], g["W_uk"], g["positions"],
+                                 mc.NOPE, mc.ROPE, mc.EPS, precision="tensor")
+    assert rel_l2(qa, qa2) < TOL

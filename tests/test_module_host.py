@@ -36,3 +36,8 @@ def test_precision_setting():
     mcc.set_precision(old)
     with pytest.raises(ValueError):
         mcc.set_precision("fp8")
+
+
+def test_packing_rejects_cpu_and_16bit_weights():
+    with pytest.raises(RuntimeError, match="CUDA"):
+        mcc.pack_q_weights(torch.zeros(64, 32), torch.zeros(32, 96), torch.zeros(4, 16, 32), 16, 8)
