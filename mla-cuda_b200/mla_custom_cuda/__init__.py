@@ -10,6 +10,12 @@ and exposes two functions (mla_kernels.cu:1688-1692):
 This module keeps those names, positional signatures, return types and error
 behaviour (shape errors raise ``RuntimeError``, like TORCH_CHECK) and runs the
 B200 kernels of ``libmla_b200.so`` through its C ABI (include/mla_b200.h).
+The four entry points q_absorbed / mla_attention (and their ``_ex`` forms) go
+through the C++ torch extension ``mla_custom_cuda._C``, built by
+``mla-cuda_b200/setup.py`` as the reference builds its own (setup.py:20-26);
+when that extension has not been built they use ``ctypes`` on the same C ABI.
+The other functions (key-shard partials and merge, weight packing, device
+status, kernel timing) always use ``ctypes``.
 Outputs and workspaces are allocated with torch's caching allocator on the
 inputs' device, and all work is enqueued on torch's current stream, as in the
 reference (mla_kernels.cu:664-667, :1528-1549).
@@ -104,6 +110,10 @@ def _load() -> ctypes.CDLL:
 
 
 _lib = _load()
+try:   # the C++ extension over the same library (optional; ctypes otherwise)
+    from . import _C  # noqa: E402
+except ImportError:
+    _C = None
 # MLA_CHECK=1: after every call, wait for the stream and raise RuntimeError if a
 # kernel recorded a device-side failure (costs a synchronisation per call).
 _checked = os.environ.get("MLA_CHECK", "0").strip() not in ("", "0")
@@ -115,6 +125,11 @@ if _precision not in _PRECISIONS:
 def library_path() -> str:
     """Path of the loaded C-ABI library."""
     return str(_LIB_PATH)
+
+
+def binding() -> str:
+    """How q_absorbed / mla_attention reach the library: "extension" or "ctypes"."""
+    return "extension" if _C is not None else "ctypes"
 
 
 def abi_version() -> int:
@@ -220,6 +235,13 @@ def _prec_code(precision: Optional[str]) -> int:
     return _PRECISIONS[p]
 
 
+def _prec_name(precision: Optional[str]) -> str:
+    p = _precision if precision is None else precision.strip().lower()
+    if p not in _PRECISIONS:
+        raise ValueError(f"precision must be one of {sorted(_PRECISIONS)}, got {precision!r}")
+    return p
+
+
 def _float_operands(name_tensors, device=None):
     dtype = None
     for name, t in name_tensors:
@@ -257,6 +279,12 @@ def q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim: int, rop
            f"{list(positions.shape) if isinstance(positions, torch.Tensor) else type(positions)})")
     _check(not positions.is_floating_point() and not positions.is_complex(),
            "positions must be an integer tensor")
+    if _C is not None:
+        with torch.cuda.device(device):
+            res = _C.q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim, rope_dim, float(eps),
+                                   _prec_name(precision))
+        _after_call(device)
+        return list(res)
     xc, Wa, g, Wb, Wk = (t.contiguous() for t in (x, W_q_a, q_norm_w, W_q_b, W_uk))
     pos = positions.to(device=device, dtype=torch.int64).contiguous()
     qa = torch.empty((B, Sq, H, R), dtype=dtype, device=device)
@@ -376,6 +404,12 @@ def mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float, cau
     _check(W_uv.dim() == 3 and W_uv.shape[0] == H and W_uv.shape[2] == R,
            f"W_uv must be [H,v_dim,kv_rank] (got {tuple(W_uv.shape)})")
     V = W_uv.shape[1]
+    if _C is not None:
+        with torch.cuda.device(device):
+            out = _C.mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, float(scale), bool(causal),
+                                      _prec_name(precision))
+        _after_call(device)
+        return out
     qa, qr, ck, pe, wv = (t.contiguous() for t in (q_absorbed, q_rope, c_kv, pe_cache, W_uv))
     out = torch.empty((B, Sq, H, V), dtype=dtype, device=device)
     dt, pc = _DTYPE_CODES[dtype], _prec_code(precision)
