@@ -44,7 +44,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1500)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c1", choices=sorted(mc.CONFIGS))
+    ap.add_argument("--config", default="c1", choices=sorted(mc.CONFIGS) + sorted(mc.SCENARIOS))
+    ap.add_argument("--scenarios", action="store_true",
+                    help="also time every PRODUCTION_SCENARIOS shape of the reference (extra 'scenarios' field)")
     ap.add_argument("--precision", default="tensor", choices=["exact", "tensor"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -231,7 +233,7 @@ def main_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    w = mc.CONFIGS[args.config]
+    w = mc.CONFIGS.get(args.config) or mc.SCENARIOS[args.config]
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     t = mc.make_inputs(w, device="cpu", gen="device", seed=0)
@@ -321,6 +323,26 @@ def parity_sample(mcc, t, w, precision, seqs):
     return res
 
 
+def time_scenarios(mcc, dev, stream):
+    """Layer forward (q_absorbed + mla_attention, eager, CUDA events) of every
+    PRODUCTION_SCENARIOS shape of the reference in both precisions."""
+    res = {}
+    for name, w in mc.SCENARIOS.items():
+        t = mc.make_inputs(w, device=dev, gen="device", seed=7)
+        row = {"batch": w.batch, "sq": w.sq, "sk": w.sk}
+        for prec in ("tensor", "exact"):
+            def step():
+                qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"],
+                                           t["positions"], w.nope, w.rope, mc.EPS, precision=prec)
+                return mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, precision=prec)
+            ms = device_timed(stream, step, 5)
+            row[prec] = {"layer_ms": ms, "tokens_per_s": w.batch * w.sq / (ms * 1e-3)}
+        res[name] = row
+        del t
+        torch.cuda.empty_cache()
+    return res
+
+
 def key_shard_c2(mcc, dev, rank, world, steps, precision):
     """Config c2 (B=4, Sk=65536) key-sharded over all ranks inside this run:
     every rank holds 1/world of every sequence's keys, the partials are
@@ -367,7 +389,7 @@ def main_ours(args):
         dist.init_process_group("nccl", device_id=dev)
     import mla_custom_cuda as mcc
 
-    w = mc.CONFIGS[args.config]
+    w = mc.CONFIGS.get(args.config) or mc.SCENARIOS[args.config]
     precision = args.precision
     B = w.batch
     shard = args.shard or ("keys" if args.config == "c2" else "batch")
@@ -544,6 +566,8 @@ def main_ours(args):
                 if prec != precision:
                     stages[prec]["e2e"] = e2e_run(prec)
 
+    scen = time_scenarios(mcc, dev, stream) if (args.scenarios and rank == 0 and world == 1) else None
+
     # ---- c2 key-sharded across all ranks (strong scaling), when several GPUs run
     key_c2 = None
     if world > 1 and shard == "batch" and not args.no_key_shard_c2:
@@ -602,6 +626,8 @@ def main_ours(args):
         }
         if key_c2 is not None:
             line["key_shard_c2"] = key_c2
+        if scen is not None:
+            line["scenarios"] = scen
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()

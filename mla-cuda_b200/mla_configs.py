@@ -66,6 +66,24 @@ CONFIGS = {
 }
 
 
+# The reference's PRODUCTION_SCENARIOS (exhaustive_benchmark_suite.py:78-173):
+# decode and speculative-decode shapes taken from public serving reports, and
+# prefill chunks. The reference runs every one without a mask (each query
+# attends all Sk keys), so these do too.
+SCENARIOS = {
+    "decode_single_user_long_ctx": Workload("decode_single_user_long_ctx", 1, 1, 65536),
+    "decode_serving_avg_ctx": Workload("decode_serving_avg_ctx", 128, 1, 4989),
+    "decode_serving_long_ctx": Workload("decode_serving_long_ctx", 128, 1, 8192),
+    "decode_serving_high_batch": Workload("decode_serving_high_batch", 256, 1, 2048),
+    "decode_speculative_2tok": Workload("decode_speculative_2tok", 64, 2, 512),
+    "decode_speculative_4tok": Workload("decode_speculative_4tok", 64, 4, 768),
+    "decode_speculative_long_ctx": Workload("decode_speculative_long_ctx", 132, 4, 4096),
+    "prefill_chat_batch": Workload("prefill_chat_batch", 8, 512, 512),
+    "prefill_chunk_2k": Workload("prefill_chunk_2k", 1, 2048, 2048),
+    "prefill_chunk_4k": Workload("prefill_chunk_4k", 1, 4096, 4096),
+}
+
+
 def positions_for(sq: int, sk: int) -> torch.Tensor:
     return torch.arange(sk - sq + 1, sk + 1, dtype=torch.int64)
 
