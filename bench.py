@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=1500)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="c1", choices=sorted(mc.CONFIGS) + sorted(mc.SCENARIOS))
+    ap.add_argument("--reference-gpu", action="store_true",
+                    help="also time the reference's own CUDA kernels (mla_kernels.cu built for sm_100a by "
+                         "oracle/build_ref.py into oracle/_ref/) on BASELINE configs c0-c3 (extra field)")
     ap.add_argument("--scenarios", action="store_true",
                     help="also time every PRODUCTION_SCENARIOS shape of the reference (extra 'scenarios' field)")
     ap.add_argument("--precision", default="tensor", choices=["exact", "tensor"])
@@ -343,6 +346,48 @@ def time_scenarios(mcc, dev, stream):
     return res
 
 
+def time_reference_gpu(mcc, dev, stream):
+    """The reference's two CUDA entry points (mla_kernels.cu, unmodified, built for
+    sm_100a) on BASELINE configs c0-c3, fp32, beside this library's exact path on
+    the same inputs; CUDA events, 10 calls after 3 warm-ups. The reference has no
+    mask, so c3 runs unmasked on both sides here."""
+    import importlib.machinery
+    import importlib.util
+    so = ROOT / "oracle" / "_ref" / "mla_ref_cuda.so"
+    if not so.exists():
+        return {"unavailable": "oracle/_ref/mla_ref_cuda.so not built (python oracle/build_ref.py)"}
+    loader = importlib.machinery.ExtensionFileLoader("mla_ref_cuda", str(so))
+    spec = importlib.util.spec_from_file_location("mla_ref_cuda", str(so), loader=loader)
+    ref = importlib.util.module_from_spec(spec)
+    loader.exec_module(ref)
+    res = {}
+    for cfg in ("c0", "c1", "c2", "c3"):
+        w = mc.CONFIGS[cfg]
+        t = mc.make_inputs(w, device=dev, gen="device", seed=11)
+
+        def ref_step():
+            qa, qr = ref.q_absorbed(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                                    w.nope, w.rope, mc.EPS)
+            return ref.mla_attention(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale)
+
+        def our_step(prec):
+            qa, qr = mcc.q_absorbed_ex(t["x"], t["W_q_a"], t["q_norm_w"], t["W_q_b"], t["W_uk"], t["positions"],
+                                       w.nope, w.rope, mc.EPS, precision=prec)
+            return mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, precision=prec)
+
+        r_ms = device_timed(stream, ref_step, 10)
+        e_ms = device_timed(stream, lambda: our_step("exact"), 10)
+        t_ms = device_timed(stream, lambda: our_step("tensor"), 10)
+        a, b = ref_step(), our_step("exact")
+        torch.cuda.synchronize()
+        res[cfg] = {"reference_cuda_ms": r_ms, "ours_exact_ms": e_ms, "ours_tensor_ms": t_ms,
+                    "exact_speedup": r_ms / e_ms, "tensor_speedup": r_ms / t_ms,
+                    "rel_l2_exact_vs_reference_cuda": float((a.double() - b.double()).norm() / a.double().norm())}
+        del t
+        torch.cuda.empty_cache()
+    return res
+
+
 def key_shard_c2(mcc, dev, rank, world, steps, precision):
     """Config c2 (B=4, Sk=65536) key-sharded over all ranks inside this run:
     every rank holds 1/world of every sequence's keys, the partials are
@@ -567,6 +612,7 @@ def main_ours(args):
                     stages[prec]["e2e"] = e2e_run(prec)
 
     scen = time_scenarios(mcc, dev, stream) if (args.scenarios and rank == 0 and world == 1) else None
+    ref_gpu = time_reference_gpu(mcc, dev, stream) if (args.reference_gpu and rank == 0 and world == 1) else None
 
     # ---- c2 key-sharded across all ranks (strong scaling), when several GPUs run
     key_c2 = None
@@ -628,6 +674,8 @@ def main_ours(args):
             line["key_shard_c2"] = key_c2
         if scen is not None:
             line["scenarios"] = scen
+        if ref_gpu is not None:
+            line["reference_gpu"] = ref_gpu
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
