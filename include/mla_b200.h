@@ -180,6 +180,41 @@ MLA_API mla_status_t mla_attention(
     void* out,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------- KV-cache write --
+ * The step upstream of the decode read. The reference has no kernel for it
+ * (its caches are inputs; the write is only mentioned,
+ * exhaustive_benchmark_suite.py:189); the arithmetic composes the reference's
+ * own rmsnorm (:252-258) and apply_rope (:210-232). For each new token (b, s):
+ *
+ *   kv = x[b, s] @ W_kv_a                               [kv_rank + rope]
+ *   c_kv    [b, slots[s]] = RMSNorm(kv[:kv_rank]) * kv_norm_w   (eps)
+ *   pe_cache[b, slots[s]] = RoPE(kv[kv_rank:], positions[s])    (theta 10000,
+ *                                                                interleaved pairs)
+ *
+ *   x          [batch, sq, hidden]        storage dtype (fp32, fp16 or bf16)
+ *   W_kv_a     [hidden, kv_rank + rope]
+ *   kv_norm_w  [kv_rank]
+ *   positions, slots  [sq] int64 on the device (same for every sequence)
+ *   c_kv       [batch, capacity, kv_rank]  written in place at the slots
+ *   pe_cache   [batch, capacity, rope]
+ *
+ * Exact precision projects in 3xTF32 (fp32 storage); tensor precision in
+ * kind::tf32; 16-bit storage in kind::f16 (fp32 accumulation either way). A
+ * slot outside [0, capacity) is not written and records code 950 in the device
+ * status (mla_device_status).
+ */
+MLA_API mla_status_t mla_kv_cache_write_workspace_size(
+    mla_dtype_t dtype, mla_precision_t precision, int64_t batch, int64_t sq,
+    int64_t hidden, int64_t kv_rank, int64_t rope, size_t* bytes);
+
+MLA_API mla_status_t mla_kv_cache_write(
+    mla_dtype_t dtype, mla_precision_t precision,
+    const void* x, const void* W_kv_a, const void* kv_norm_w,
+    const int64_t* positions, const int64_t* slots,
+    int64_t batch, int64_t sq, int64_t hidden, int64_t kv_rank, int64_t rope,
+    int64_t capacity, double eps,
+    void* c_kv, void* pe_cache, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------ key-sharded attention --
  * No counterpart in the reference (it is single-GPU). For long contexts the
  * keys of every sequence can be split across GPUs: each GPU runs

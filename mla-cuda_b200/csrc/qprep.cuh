@@ -42,6 +42,9 @@ mla_status_t pack_q_weights(const float* W_q_a, const float* W_q_b, const float*
 size_t qprep_packed_workspace(const QArgs& a);
 mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st);
 
+// KV-cache write (kv_write.cu)
+bool kv_write_supported(mla_dtype_t dt, int64_t hidden, int64_t kv_rank, int64_t rope);
+
 template <typename T> size_t attn_exact_workspace(const AArgs& a);
 template <typename T> mla_status_t attn_exact(const AArgs& a, cudaStream_t st);
 

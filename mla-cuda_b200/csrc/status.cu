@@ -107,8 +107,10 @@ mla_status_t mla_device_status(void* stream, int* code) {
     *code = v;
     if (v != 0)
         return set_error(MLA_ERR_DEVICE,
-                         "MLA: a kernel gave up on a bounded wait (code %d: %s); its outputs are invalid", v,
-                         v >= kErrSelftestTimeout ? "wait self-test" : v >= 200 ? "tensor-core GEMM" : "decode attention");
+                         "MLA: device-side failure (code %d: %s); the outputs of that call are invalid", v,
+                         v == 950 ? "KV-cache write: slot outside the cache, not written"
+                         : v >= kErrSelftestTimeout ? "wait self-test" : v >= 200 ? "tensor-core GEMM"
+                                                                                   : "decode attention");
     return MLA_OK;
 }
 

@@ -45,7 +45,7 @@ __all__ = [
     "mla_attention_partial", "lse_combine",
     "set_precision", "get_precision", "library_path", "abi_version",
     "device_status", "clear_device_status", "check_device", "set_wait_limit_ns", "wait_selftest",
-    "kernel_timing", "pack_q_weights", "q_absorbed_packed", "PackedQWeights",
+    "kernel_timing", "kv_cache_write", "pack_q_weights", "q_absorbed_packed", "PackedQWeights",
 ]
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmla_b200.so"
@@ -102,6 +102,12 @@ def _load() -> ctypes.CDLL:
     lib.mla_q_absorbed_packed.restype = ctypes.c_int
     lib.mla_q_absorbed_packed.argtypes = ([ctypes.c_int] + [_c_vp] * 4 + [_c_i64] * 8
                                           + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
+    lib.mla_kv_cache_write_workspace_size.restype = ctypes.c_int
+    lib.mla_kv_cache_write_workspace_size.argtypes = [ctypes.c_int, ctypes.c_int] + [_c_i64] * 5 + [
+        ctypes.POINTER(_c_size)]
+    lib.mla_kv_cache_write.restype = ctypes.c_int
+    lib.mla_kv_cache_write.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_vp] * 5 + [_c_i64] * 6
+                                       + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
     lib.mla_timing_enable.restype = ctypes.c_int
     lib.mla_timing_enable.argtypes = [ctypes.c_int]
     lib.mla_timing_read.restype = ctypes.c_int
@@ -304,6 +310,47 @@ def q_absorbed_ex(x, W_q_a, q_norm_w, W_q_b, W_uk, positions, nope_dim: int, rop
     _raise_status(st, "q_absorbed")
     _after_call(device)
     return [qa, qr]
+
+
+def kv_cache_write(x, W_kv_a, kv_norm_w, positions, slots, c_kv, pe_cache, eps: float = 1e-6,
+                   precision: Optional[str] = None) -> None:
+    """Writes the new tokens' KV-cache rows in place: for token (b, s),
+    c_kv[b, slots[s]] = RMSNorm((x @ W_kv_a)[..., :kv_rank]) * kv_norm_w and
+    pe_cache[b, slots[s]] = RoPE((x @ W_kv_a)[..., kv_rank:], positions[s]).
+
+    The reference has no write path (its caches are inputs; the step is only
+    mentioned at exhaustive_benchmark_suite.py:189); this composes its rmsnorm
+    and apply_rope. x [B,Sq,hidden], W_kv_a [hidden, kv_rank+rope],
+    kv_norm_w [kv_rank], positions / slots [Sq] integers, c_kv [B,cap,kv_rank],
+    pe_cache [B,cap,rope]; fp32 / fp16 / bf16. A slot outside [0, cap) is not
+    written and is reported by device_status() (code 950)."""
+    dtype, device = _float_operands([("x", x), ("W_kv_a", W_kv_a), ("kv_norm_w", kv_norm_w), ("c_kv", c_kv),
+                                     ("pe_cache", pe_cache)])
+    _check(x.dim() == 3 and W_kv_a.dim() == 2 and W_kv_a.shape[0] == x.shape[2], "W_kv_a must be [hidden, kv_rank+rope]")
+    B, Sq, hidden = x.shape
+    _check(c_kv.dim() == 3 and c_kv.shape[0] == B, "c_kv must be [B, capacity, kv_rank]")
+    cap, R = c_kv.shape[1], c_kv.shape[2]
+    D = W_kv_a.shape[1] - R
+    _check(D >= 0 and tuple(pe_cache.shape) == (B, cap, D), "pe_cache must be [B, capacity, rope]")
+    _check(kv_norm_w.dim() == 1 and kv_norm_w.shape[0] == R, "kv_norm_w must be [kv_rank]")
+    _check(c_kv.is_contiguous() and pe_cache.is_contiguous(), "the caches must be contiguous (written in place)")
+    for name, v in (("positions", positions), ("slots", slots)):
+        _check(isinstance(v, torch.Tensor) and v.dim() == 1 and v.shape[0] == Sq and not v.is_floating_point(),
+               f"{name} must be a 1-D integer tensor of length Sq")
+    xc, W, g = x.contiguous(), W_kv_a.contiguous(), kv_norm_w.contiguous()
+    pos = positions.to(device=device, dtype=torch.int64).contiguous()
+    sl = slots.to(device=device, dtype=torch.int64).contiguous()
+    dt, pc = _DTYPE_CODES[dtype], _prec_code(precision)
+    nbytes = _c_size(0)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_kv_cache_write_workspace_size(dt, pc, B, Sq, hidden, R, D, ctypes.byref(nbytes)),
+                      "kv_cache_write")
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=device)
+        st = _lib.mla_kv_cache_write(dt, pc, xc.data_ptr(), W.data_ptr(), g.data_ptr(), pos.data_ptr(), sl.data_ptr(),
+                                     B, Sq, hidden, R, D, cap, float(eps), c_kv.data_ptr(), pe_cache.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), _stream_of(device))
+    _raise_status(st, "kv_cache_write")
+    _after_call(device)
 
 
 class PackedQWeights:

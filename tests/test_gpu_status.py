@@ -48,7 +48,7 @@ def test_wait_that_runs_out_is_reported(mcc):
     mcc.set_wait_limit_ns(1_000_000, DEV)
     mcc.wait_selftest(DEV)
     assert mcc.device_status(DEV) == 900
-    with pytest.raises(RuntimeError, match="bounded wait"):
+    with pytest.raises(RuntimeError, match="device-side failure"):
         mcc.check_device(DEV)
     mcc.clear_device_status(DEV)
     assert mcc.device_status(DEV) == 0

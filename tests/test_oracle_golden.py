@@ -93,3 +93,18 @@ def test_rope_inverse_frequencies_are_correctly_rounded():
         mine = np.array([np.float32(1.0) / np.float32(10000.0 ** (2 * j / rope)) for j in range(rope // 2)],
                         dtype=np.float32)
         assert np.array_equal(torch_inv, mine)
+
+
+def test_kv_cache_rows_compose_the_pinned_functions():
+    """oracle.kv_cache_rows is the reference's rmsnorm and apply_rope (both pinned
+    by the goldens above) applied to x @ W_kv_a."""
+    from oracle import mla_oracle as orc
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(2, 3, 64, generator=g, dtype=torch.float64)
+    W = torch.randn(64, 40, generator=g, dtype=torch.float64)
+    gain = torch.rand(32, generator=g, dtype=torch.float64)
+    pos = torch.tensor([5, 6, 7])
+    c, pe = orc.kv_cache_rows(x, W, gain, pos, kv_rank=32)
+    kv = x @ W
+    assert torch.equal(c, orc.rmsnorm(kv[..., :32], gain))
+    assert torch.equal(pe, orc.apply_rope(kv[..., 32:].unsqueeze(2), pos, 8).squeeze(2))
