@@ -144,8 +144,10 @@ mla_status_t kv_write(const void* x, const void* W_kv_a, const void* kv_norm_w, 
     g.split3 = exact && std::is_same<T, float>::value;
     MLA_TRY(tc_gemm<T>(g, st));
     KvRope<T> tab{};
+    // 1 / fp32(10000^(2j/rope)) in fp32, as the reference's apply_rope computes its
+    // inverse frequencies (an fp32 power, then an fp32 division)
     for (int64_t j = 0; j < rope / 2; ++j)
-        tab.inv_freq[j] = float(1.0 / std::pow(10000.0, double(2 * j) / double(rope)));
+        tab.inv_freq[j] = 1.0f / float(std::pow(10000.0, double(2 * j) / double(rope)));
     kv_norm_rope_write_kernel<T><<<unsigned(M), 256, 0, st>>>(
         P, p.split, M, sq, kv_rank, rope, static_cast<const T*>(kv_norm_w), positions, slots, capacity, float(eps),
         tab, static_cast<T*>(c_kv), static_cast<T*>(pe_cache), &dst->code);
