@@ -93,3 +93,56 @@ def test_attention_rejects_missing_workspace(lib):
                            i64(64), i64(128), ctypes.c_double(13.8), 0, fake, vp(0), ctypes.c_size_t(0),
                            vp(0))
     assert st == 3   # MLA_ERR_WORKSPACE, detected before any device work
+
+
+def _size_t():
+    return ctypes.c_size_t(0)
+
+
+def test_pack_q_weights_size_and_validation(lib):
+    f = lib.mla_pack_q_weights_size
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int] + [ctypes.c_int64] * 6 + [ctypes.POINTER(ctypes.c_size_t)]
+    n = _size_t()
+    assert f(0, 7168, 1536, 128, 128, 64, 512, ctypes.byref(n)) == 0
+    # bf16 copies of W_q_a, W_q_b, W_uk, each part 256-byte aligned
+    expect = 7168 * 1536 * 2 + 1536 * 128 * 192 * 2 + 128 * 128 * 512 * 2
+    assert expect <= n.value < expect + 3 * 256
+    assert f(3, 7168, 1536, 128, 128, 64, 512, ctypes.byref(n)) == 2      # bf16 storage: MLA_ERR_UNSUPPORTED
+    assert f(0, 7168, 1536, 128, 128, 63, 512, ctypes.byref(n)) == 1      # odd rope: invalid argument
+    g = lib.mla_pack_q_weights
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 6 + [ctypes.c_void_p, ctypes.c_size_t,
+                                                                                     ctypes.c_void_p]
+    assert g(0, None, None, None, 7168, 1536, 128, 128, 64, 512, None, 0, None) == 1   # null pointers
+
+
+def test_q_absorbed_packed_validation(lib):
+    f = lib.mla_q_absorbed_packed_workspace_size
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int] + [ctypes.c_int64] * 8 + [ctypes.POINTER(ctypes.c_size_t)]
+    n = _size_t()
+    assert f(0, 0, 1, 7168, 1536, 128, 128, 64, 512, ctypes.byref(n)) == 0 and n.value == 0   # empty batch
+    assert f(2, 4, 1, 7168, 1536, 128, 128, 64, 512, ctypes.byref(n)) == 2                   # fp16: unsupported
+
+
+def test_kv_cache_write_validation(lib):
+    f = lib.mla_kv_cache_write_workspace_size
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int, ctypes.c_int] + [ctypes.c_int64] * 5 + [ctypes.POINTER(ctypes.c_size_t)]
+    n = _size_t()
+    assert f(0, 0, 0, 1, 7168, 512, 64, ctypes.byref(n)) == 0 and n.value == 0
+    assert f(1, 0, 4, 1, 7168, 512, 64, ctypes.byref(n)) == 2      # fp64: unsupported
+    assert f(0, 0, 4, 1, 7168, 2048, 64, ctypes.byref(n)) == 2     # kv_rank above 1024
+    assert f(0, 7, 4, 1, 7168, 512, 64, ctypes.byref(n)) == 2      # unknown precision
+    w = lib.mla_kv_cache_write
+    w.restype = ctypes.c_int
+    w.argtypes = ([ctypes.c_int, ctypes.c_int] + [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 6
+                  + [ctypes.c_double] + [ctypes.c_void_p] * 3 + [ctypes.c_size_t, ctypes.c_void_p])
+    assert w(0, 0, None, None, None, None, None, 1, 1, 7168, 512, 64, 16, 1e-6, None, None, None, 0, None) == 1
+
+
+def test_status_strings_cover_every_code(lib):
+    lib.mla_status_string.restype = ctypes.c_char_p
+    names = [lib.mla_status_string(c).decode() for c in range(6)]
+    assert names[5] == "device-side failure" and len(set(names)) == 6
