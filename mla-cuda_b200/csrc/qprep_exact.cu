@@ -687,12 +687,15 @@ QPPlan make_pplan(const QArgs& a) {
     const int64_t bk = tc_gemm_bk<B16>();
     const int64_t mt = ceil_div(M, 128);
     p.split1 = tc_split(mt * ceil_div(a.q_lora, 128), M, a.hidden, bk, p.chunk1);
-    p.split2 = tc_split(mt * ceil_div(ncols, 128), M, a.q_lora, bk, p.chunk2);
+    // 2a2 is not split over K: its epilogue splits q per head and applies the RoPE
+    p.split2 = 1;
+    p.chunk2 = a.q_lora;
+    (void)ncols;
     size_t off = 0;
     p.off_x = off;     off = align_up(off + size_t(M) * a.hidden * sizeof(B16), 256);
     p.off_p1 = off;    off = align_up(off + size_t(p.split1) * M * a.q_lora * sizeof(float), 256);
     p.off_qlat = off;  off = align_up(off + size_t(M) * a.q_lora * sizeof(B16), 256);
-    p.off_p2 = off;    off = align_up(off + size_t(p.split2) * M * ncols * sizeof(float), 256);
+    p.off_p2 = off;
     p.off_qnope = off; off = align_up(off + size_t(M) * a.heads * a.nope * sizeof(B16), 256);
     p.total = off;
     return p;
@@ -703,7 +706,7 @@ QPPlan make_pplan(const QArgs& a) {
 bool qprep_packed_supported(const QArgs& a) {
     const int64_t ncols = a.heads * (a.nope + a.rope);
     return a.q_lora % 32 == 0 && ncols % 32 == 0 && a.kv_rank % 32 == 0 && a.hidden % 8 == 0 && a.q_lora % 8 == 0 &&
-           a.nope % 8 == 0 && a.rope % 4 == 0 && a.nope % 4 == 0 && a.q_lora <= 4096 && a.batch * a.sq > 0 &&
+           a.nope % 32 == 0 && a.rope % 32 == 0 && a.rope <= 128 && a.q_lora <= 4096 && a.batch * a.sq > 0 &&
            (a.batch * a.sq * a.hidden) % 4 == 0;
 }
 
@@ -737,7 +740,6 @@ mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st) {
     B16* x16 = reinterpret_cast<B16*>(ws + p.off_x);
     float* P1 = reinterpret_cast<float*>(ws + p.off_p1);
     B16* q_lat = reinterpret_cast<B16*>(ws + p.off_qlat);
-    float* P2 = reinterpret_cast<float*>(ws + p.off_p2);
     B16* q_nope = reinterpret_cast<B16*>(ws + p.off_qnope);
     MLA_TRY(cast_bf16(static_cast<const float*>(a.x), x16, M * a.hidden, st));
 
@@ -757,21 +759,23 @@ mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st) {
         MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
     }
 
-    TcGemm g2{};   // 2a2: q_lat [M, q_lora] @ W_q_b [q_lora, H*(nope+rope)]
+    // 2a2: q_lat [M, q_lora] @ W_q_b [q_lora, H*(nope+rope)]; the epilogue stores
+    // q_nope (bf16) and the rotated q_rope (fp32) directly
+    GemmRopeEpilogue re{};
+    re.q_nope = q_nope;
+    re.q_rope = static_cast<float*>(a.q_rope);
+    re.positions = a.positions;
+    re.sq = a.sq; re.heads = a.heads; re.nope = a.nope; re.rope = a.rope;
+    for (int64_t j = 0; j < a.rope / 2; ++j)   // 1 / fp32(10000^(2j/rope)) in fp32, as apply_rope
+        re.inv_freq[j] = 1.0f / float(std::pow(10000.0, double(2 * j) / double(a.rope)));
+    TcGemm g2{};
     g2.A = q_lat; g2.a_dims[0] = a.q_lora; g2.a_dims[1] = 1; g2.a_dims[2] = M; g2.a_ld[0] = a.q_lora; g2.a_ld[1] = a.q_lora;
     g2.B = pk + l.off_qb; g2.b_mn = true; g2.b_dims[0] = ncols; g2.b_dims[1] = a.q_lora; g2.b_dims[2] = 1;
     g2.b_ld[0] = ncols; g2.b_ld[1] = ncols * a.q_lora;
-    g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = p.split2; g2.spb = p.split2; g2.k_chunk = p.chunk2;
-    g2.C = P2; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err;
+    g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = 1; g2.spb = 1; g2.k_chunk = a.q_lora;
+    g2.C = nullptr; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err;
+    g2.rope_epi = &re;
     MLA_TRY(tc_gemm<B16>(g2, st));
-
-    RopeTable<float> tab{};
-    for (int64_t j = 0; j < a.rope / 2; ++j) {
-        const double pw = std::pow(10000.0, double(2 * j) / double(a.rope));
-        tab.inv_freq[j] = 1.0f / float(pw);
-    }
-    MLA_TRY((launch_rope_gather<float, B16>(P2, p.split2, a.positions, q_nope, static_cast<float*>(a.q_rope), M, a.sq,
-                                            a.heads, a.nope, a.rope, tab, nullptr, st)));
 
     TcGemm g3{};   // 2c: per head, q_nope[:, h, :] @ W_uk[h], fp32 output
     g3.A = q_nope; g3.a_dims[0] = a.nope; g3.a_dims[1] = a.heads; g3.a_dims[2] = M;

@@ -379,7 +379,8 @@ struct Units {
 
 template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
-    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Run r, const Units U)
+    const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Run r, const Units U,
+    const __grid_constant__ GemmRopeEpilogue re, const int use_re)
 {
     constexpr int S = pstages<BN>();
     constexpr int BK = tc_gemm_bk<T>();
@@ -516,6 +517,46 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
                 }
                 const int64_t n = n0 + c * 32;
                 if (m >= r.M || n >= r.N) continue;
+                if (use_re) {   // 2a2 epilogue: split per head, RoPE on the rope part
+                    const int64_t qk = re.nope + re.rope;
+                    const int64_t h = n / qk, o = n - h * qk;
+                    if (o < re.nope) {
+                        uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(re.q_nope) +
+                                                              (m * re.heads + h) * re.nope + o);
+                        for (int e = 0; e < 4; ++e) {
+                            uint32_t w[4];
+                            for (int hh = 0; hh < 4; ++hh) {
+                                const float lo_ = __uint_as_float(v[8 * e + 2 * hh]);
+                                const float hi = __uint_as_float(v[8 * e + 2 * hh + 1]);
+                                if constexpr (std::is_same<T, __half>::value) {
+                                    __half2 h2 = __floats2half2_rn(lo_, hi);
+                                    w[hh] = *reinterpret_cast<uint32_t*>(&h2);
+                                } else {
+                                    w[hh] = pack_bf16(lo_, hi);
+                                }
+                            }
+                            dst[e] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    } else {
+                        const int64_t ro = o - re.nope;                 // first rope dim of this chunk
+                        const float pos = float(re.positions[m % re.sq]);
+                        float4* dst = reinterpret_cast<float4*>(re.q_rope + (m * re.heads + h) * re.rope + ro);
+                        for (int e = 0; e < 8; ++e) {
+                            float out[4];
+                            for (int pp = 0; pp < 2; ++pp) {
+                                const int j = int(ro / 2) + 2 * e + pp;
+                                const float ang = pos * re.inv_freq[j];
+                                const float cs = cosf(ang), sn = sinf(ang);
+                                const float ev = __uint_as_float(v[4 * e + 2 * pp]);
+                                const float od = __uint_as_float(v[4 * e + 2 * pp + 1]);
+                                out[2 * pp] = ev * cs - od * sn;
+                                out[2 * pp + 1] = ev * sn + od * cs;
+                            }
+                            dst[e] = make_float4(out[0], out[1], out[2], out[3]);
+                        }
+                    }
+                    continue;
+                }
                 const int64_t off = m * r.c_ldm + int64_t(z) * r.c_ldz + n;
                 if (!r.c_is_t || std::is_same<T, float>::value) {
                     float4* dst = reinterpret_cast<float4*>(static_cast<float*>(r.C) + off);
@@ -573,7 +614,9 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
     const size_t smem = psmem_bytes<BN>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     const int64_t grid = U.total < sm_count() ? U.total : sm_count();
-    kern<<<unsigned(grid), kThreads, smem, st>>>(ta, tb, r, U);
+    GemmRopeEpilogue re{};
+    if (g.rope_epi) re = *g.rope_epi;
+    kern<<<unsigned(grid), kThreads, smem, st>>>(ta, tb, r, U, re, g.rope_epi ? 1 : 0);
     return check_launch("tensor-core GEMM (persistent)");
 }
 
@@ -625,6 +668,14 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
             if (g.split3) return tcg::launch<T, 128, true>(g, st);
         } else {
             if (g.split3) return set_error(MLA_ERR_UNSUPPORTED, "MLA: 3xTF32 needs fp32 operands");
+        }
+        if (g.rope_epi) {
+            const GemmRopeEpilogue& e = *g.rope_epi;
+            if (g.spb != 1 || g.Z != 1 || e.nope % 32 || e.rope % 32 || e.rope / 2 > 64 ||
+                g.N != e.heads * (e.nope + e.rope))
+                return set_error(MLA_ERR_UNSUPPORTED, "MLA: RoPE epilogue needs no split-K and 32-aligned parts");
+            if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
+            return tcg::launch_persist<T, 128>(g, st);
         }
         if (g.K2 == 0 && !g.rowmax && !tc_gemm_classic()) {
             if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);

@@ -6,6 +6,21 @@
 
 namespace mla {
 
+// Optional epilogue of the persistent kernel for the q up-projection (2a2):
+// instead of storing C, each row m's columns are split per head h into the nope
+// part, stored to q_nope[m, h, :] in the operand dtype (the left operand of 2c),
+// and the rope part, rotated by positions[m % sq] * inv_freq[j] (interleaved
+// pairs, cos / sin in fp32 as the reference's apply_rope computes them for fp32
+// storage) and stored to q_rope[m, h, :] in fp32. Needs N = heads*(nope+rope),
+// nope and rope multiples of 32, and no split-K.
+struct GemmRopeEpilogue {
+    void* q_nope;
+    float* q_rope;
+    const int64_t* positions;
+    int64_t sq, heads, nope, rope;
+    float inv_freq[64];
+};
+
 // C[z][m][n] = sum_k A[z][m][k] * B[z][k][n], accumulated in fp32 on the tensor
 // cores (kind::tf32 for fp32 operands, kind::f16 for bf16 / fp16).
 //   A : 3-D tensor, element (k, y, m) at k + y*a_ld[0] + m*a_ld[1] with dims
@@ -38,6 +53,7 @@ struct TcGemm {
     // columns n < n_valid (fp32 output; ntiles = ceil(N / bn))
     float* rowmax; int64_t n_valid;
     int* err;        // device error word (bounded waits)
+    const GemmRopeEpilogue* rope_epi;   // optional (persistent form only); C is unused then
 };
 
 template <typename T> mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st);
