@@ -18,8 +18,9 @@
 //   * loads only its own dims of the tile (TMA), once from HBM;
 //   * computes a partial score S_r = Q[:, dims_r] . K[:, dims_r]^T on the
 //     tensor cores (M = 128 heads, N = 64 keys, K = 288) into TMEM;
-//   * swaps S_r with its peer through distributed shared memory, so both
-//     hold S = S_0 + S_1 bit-identically and run the same online softmax;
+//   * swaps S_r with its peer through distributed shared memory, in log2
+//     units rounded to fp16; both CTAs round both halves the same way, so both
+//     hold the same S = S_0 + S_1 and run the same online softmax;
 //   * accumulates its half of the context, O_r += P . V[:, 256r:256r+256]
 //     (M = 128, N = 256, K = 64) in TMEM. The same shared-memory tile is the
 //     K-major B operand of the score MMA and the MN-major B operand of P.V.
@@ -86,10 +87,11 @@ constexpr int kStgRows = 16;                // an fp32 staging buffer holds a qu
 constexpr int kStgLatBytes = kStgRows * kHalf * 4;
 constexpr int kStgBytes = kStgRows * (kHalf + kRopeHalf) * 4;
 constexpr int kXBufs = 2;                   // partial-score exchange buffers (flow-controlled)
-// one exchange buffer: the 128 rows x 64 fp32 partial scores of a tile, stored
-// chunk-major (16-byte chunk e of row r at (e*128 + r)*16), so that a warp's 32
-// rows write and read 512 contiguous bytes per instruction
-constexpr int kXBytes = kHeads * NK * 4;
+// one exchange buffer: the 128 rows x 64 partial scores of a tile, in log2 units
+// (times log2(e)/scale) rounded to fp16, stored chunk-major (16-byte chunk e =
+// keys 8e..8e+7 of row r at (e*128 + r)*16), so that a warp's 32 rows write and
+// read 512 contiguous bytes per instruction
+constexpr int kXBytes = kHeads * NK * 2;
 constexpr int kQRopeBytes = kHeads * kRopeHalf * 2;   // rope query slice: 128 rows of 64 B, 64B swizzle
 
 // TMEM columns: O half, kSBufs score / probability buffers, the query slice.
@@ -103,18 +105,21 @@ static_assert(kTmemQ + kHalf / 2 == kTmemCols, "TMEM budget");
 enum : int { ERR_TIMEOUT_BASE = 100 };
 
 template <typename T> struct Traits;
+// Staging depth: fp32 tiles stream through kStages quarter-tile buffers, whose
+// bytes are what the SM has in flight from HBM; four (a whole tile) cover the
+// load latency at the tile rate the rest of the pipeline sustains.
 template <> struct Traits<float> {
     static constexpr bool kConvert = true;
     static constexpr int kSlots = 3;
-    static constexpr int kStages = 2;
+    static constexpr int kStages = 4;
     static constexpr uint32_t kFmt = 1;     // bf16 operands
 };
 template <> struct Traits<__nv_bfloat16> {
-    static constexpr bool kConvert = false; static constexpr int kSlots = 4; static constexpr int kStages = 0;
+    static constexpr bool kConvert = false; static constexpr int kSlots = 5; static constexpr int kStages = 0;
     static constexpr uint32_t kFmt = 1;
 };
 template <> struct Traits<__half> {
-    static constexpr bool kConvert = false; static constexpr int kSlots = 4; static constexpr int kStages = 0;
+    static constexpr bool kConvert = false; static constexpr int kSlots = 5; static constexpr int kStages = 0;
     static constexpr uint32_t kFmt = 0;     // fp16 operands
 };
 
@@ -238,6 +243,8 @@ struct Bars {
     int abort;
 };
 static_assert(sizeof(Bars) <= 4096, "barrier area");
+static_assert(Traits<float>::kSlots <= 6 && Traits<float>::kStages <= 6 && Traits<__nv_bfloat16>::kSlots <= 6 &&
+              Traits<__half>::kSlots <= 6, "barrier arrays");
 
 // 64B-swizzled byte offset of 16-byte unit u (0..3) of row r in a region of
 // 64-byte rows (the layout TMA's SWIZZLE_64B writes and the MMA descriptor's
@@ -245,6 +252,20 @@ static_assert(sizeof(Bars) <= 4096, "barrier area");
 __device__ __forceinline__ uint32_t swz64(uint32_t r, uint32_t u) { return r * 64u + ((u ^ ((r >> 1) & 3u)) << 4); }
 // 128B-swizzled byte offset of 16-byte unit u (0..7) of row r (128-byte rows).
 __device__ __forceinline__ uint32_t swz128(uint32_t r, uint32_t u) { return r * 128u + ((u ^ (r & 7u)) << 4); }
+
+// Two partial scores in log2 units (times c = log2(e)/scale), rounded to fp16
+// (finite: saturates at +-65504) and packed (lo, hi). Both CTAs of a pair round
+// their own and the peer's partial the same way, so both hold the same sums.
+__device__ __forceinline__ uint32_t pack_x16(float lo, float hi, float c) {
+    uint32_t d;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi * c), "f"(lo * c));
+    return d;
+}
+__device__ __forceinline__ float2 unpack_x16(uint32_t v) {
+    __half2 h;
+    memcpy(&h, &v, 4);
+    return __half22float2(h);
+}
 
 template <typename T>
 __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
@@ -293,11 +314,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
         // the softmax warp that consumed the buffer's previous tile)
         for (int i = 0; i < kXBufs; ++i)
             for (int w = 0; w < 4; ++w) {
-#ifdef MLA_EXP_HALFPUSH
                 mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(32 * NK * 2));
-#else
-                mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(32 * NK * 4));
-#endif
                 mbar_arrive_expect_tx(&bars->x_free[i][w], 4u);   // the signal freeing the buffer for tile i+2
             }
         bars->abort = 0;
@@ -448,6 +465,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
             const int row = threadIdx.x - 256;               // head
             const int wq = warp & 3;
             const uint32_t lane_off = uint32_t(wq * 32) << 16;
+            const float c = p.c_log2;
             // peer addresses of my exchange row (chunk 0) and of my warp's exchange
             // barriers (buffer 0; buffer b is at +b*kXBytes / +b*4*8 bytes)
             const uint32_t xpeer0 = map_peer(xbuf + row * 4, peer);
@@ -522,23 +540,22 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                                                        ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true))))
                     break;
                 if (lane == 0 && i >= kXBufs && i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_free[xb][wq], 4u);
-                // st.async pushes my partial, counted on the peer's barrier
+                // st.async pushes my partial (log2 units, fp16), counted on the peer's barrier
 #pragma unroll
                 for (int h = 0; h < NK / 32; ++h) {   // 32 keys at a time
                     uint32_t sr[32];
                     tmem_ld32(tmem + lane_off + kTmemS + sb * NK + h * 32, sr);
                     tmem_ld_wait();
-#ifdef MLA_EXP_HALFPUSH
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-#else
+                    for (int e = 0; e < 4; ++e) {      // chunk h*4+e: keys 32h+8e .. +7
+                        uint32_t w[4];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-#endif
-                        st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + uint32_t(h * 8 + e) * (kHeads * 16),
-                                    __uint_as_float(sr[4 * e]), __uint_as_float(sr[4 * e + 1]),
-                                    __uint_as_float(sr[4 * e + 2]), __uint_as_float(sr[4 * e + 3]),
-                                    xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
+                        for (int q = 0; q < 4; ++q)
+                            w[q] = pack_x16(__uint_as_float(sr[8 * e + 2 * q]), __uint_as_float(sr[8 * e + 2 * q + 1]), c);
+                        st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + uint32_t(h * 4 + e) * (kHeads * 16),
+                                    __uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]),
+                                    __uint_as_float(w[3]), xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
+                    }
                 }
                 tc_fence_before();
                 mbar_arrive(&bars->s_read[sb]);
@@ -558,14 +575,15 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
             // columns of the O half; the sums are added at the epilogue. After both
             // have read the exchange buffer, the first warp announces the bytes of
             // the buffer's next tile and tells the peer's exchange warp (a 4-byte
-            // st.async completing its x_free barrier) that it may push them.
+            // st.async completing its x_free barrier) that it may push them. Scores are
+            // in log2 units here (the exchanged partials are).
             const int wq = warp & 3;
             const int hk = warp >= 12 ? 1 : 0;                // key half
             const int row = wq * 32 + lane;                  // head
             const uint32_t lane_off = uint32_t(wq * 32) << 16;
             const uint32_t bar_id = 1u + uint32_t(wq);
             const float c = p.c_log2;
-            const float tau = 8.0f / c;                      // lazy rescale threshold (raw units)
+            const float tau = 8.0f;                          // lazy rescale threshold (log2 units)
             // peer addresses of this quarter's x_free barrier and landing word
             // (buffer 0; buffer b is at +b*4*8 / +b*4*4 bytes)
             const uint32_t xfree_peer0 = map_peer(&bars->x_free[0][wq], peer);
@@ -591,19 +609,31 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     break;
                 if (warp == 4 && lane == 0) MLA_TL(4, i);
                 // my partial of my 32 keys (the score buffer is not reused before P.V(i)
-                // is issued) plus the peer's partial
+                // is issued), rounded as the peer rounded the one it pushed, plus the
+                // peer's partial
                 MLA_PROF(const long long t_fi = clock64();)
                 float s[32];
-                tmem_ld32(tmem + lane_off + kTmemS + sb * NK + hk * 32, *reinterpret_cast<uint32_t(*)[32]>(s));
-                const float* xr = xbuf + xb * (kHeads * NK) + row * 4;
-                tmem_ld_wait();
+                {
+                    uint32_t sr[32];
+                    tmem_ld32(tmem + lane_off + kTmemS + sb * NK + hk * 32, sr);
+                    const uint4* xr = reinterpret_cast<const uint4*>(
+                        reinterpret_cast<const unsigned char*>(xbuf) + xb * kXBytes + (hk * 4 * kHeads + row) * 16);
+                    uint4 pv[4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float4 pv = *reinterpret_cast<const float4*>(xr + (hk * 8 + e) * (kHeads * 4));
-                    s[4 * e] += pv.x;
-                    s[4 * e + 1] += pv.y;
-                    s[4 * e + 2] += pv.z;
-                    s[4 * e + 3] += pv.w;
+                    for (int e = 0; e < 4; ++e) pv[e] = xr[e * kHeads];
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const uint32_t pw[4] = {pv[e].x, pv[e].y, pv[e].z, pv[e].w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const int k = 8 * e + 2 * q;
+                            const float2 mine = unpack_x16(pack_x16(__uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), c));
+                            const float2 peer = unpack_x16(pw[q]);
+                            s[k] = mine.x + peer.x;
+                            s[k + 1] = mine.y + peer.y;
+                        }
+                    }
                 }
                 MLA_PROF(wacc[20] += clock64() - t_fi; const long long t_f1 = clock64();)
                 const int64_t key0 = it.j * NK + hk * 32;
@@ -631,11 +661,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 // a maximum that depends on every value it read): announce the bytes of
                 // the buffer's next tile (i+2) and free it for the peer's push.
                 if (hk == 0 && lane == 0) {
-    #ifdef MLA_EXP_HALFPUSH
-                if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 2));
-#else
-                if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 4));
-#endif
+                    if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 2));
                     st_async_b32(sink_peer0 + uint32_t(xb) * 16u, mt, xfree_peer0 + uint32_t(xb) * 32u);
                 }
                 if (first) {
@@ -651,7 +677,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                         break;
                     tc_fence_after();
                     mt = fmaxf(mt, m_run);
-                    const float alpha = ex2((m_run - mt) * c);
+                    const float alpha = ex2(m_run - mt);
 #pragma unroll 1
                     for (int c32 = 0; c32 < kHalf / 64; ++c32) {
                         uint32_t o[32];
@@ -666,13 +692,13 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     m_run = mt;
                 }
                 MLA_PROF(wacc[21] += clock64() - t_f1; const long long t_f2 = clock64();)
-                const float mc = m_run * c;
+                const float mc = m_run;
                 uint32_t pk[16];
                 float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
-                    const float p0 = ex2(fmaf(s[e], c, -mc));
-                    const float p1 = ex2(fmaf(s[e + 1], c, -mc));
+                    const float p0 = ex2(s[e] - mc);
+                    const float p1 = ex2(s[e + 1] - mc);
                     ls[(e >> 1) & 3] += p0 + p1;
                     if constexpr (Tr::kFmt == 0) {
                         __half2 h2 = __floats2half2_rn(p0, p1);
@@ -719,7 +745,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     bars->xl[hk * kHeads + row] = l_run;
                     named_bar_sync(bar_id, 64);
                     if (rank == 0 && hk == 0) {
-                        p.ml[(slot * kHeads + row) * 2] = m_run * c;
+                        p.ml[(slot * kHeads + row) * 2] = m_run;
                         p.ml[(slot * kHeads + row) * 2 + 1] = l_run + bars->xl[kHeads + row];
                     }
                     tc_fence_before();
