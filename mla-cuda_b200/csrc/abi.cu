@@ -45,6 +45,14 @@ int sm_count() {
     return cached[dev];
 }
 
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("MLA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 namespace {
 
 mla_status_t validate_q(mla_dtype_t dtype, mla_precision_t prec, int64_t batch, int64_t sq, int64_t hidden,

@@ -8,6 +8,8 @@
 #include <stdint.h>
 #include <stddef.h>
 
+#include <utility>
+
 #include "mla_b200.h"
 
 namespace mla {
@@ -61,6 +63,35 @@ mla_status_t check_launch(const char* what);
 
 // Number of SMs of the current device, cached per device.
 int sm_count();
+
+// Programmatic dependent launch. The layer's kernels are launched with the
+// programmatic-serialization attribute, so a kernel's CTAs may start while its
+// predecessor on the stream is still finishing. Each such kernel does only
+// setup that touches no global data (barriers, TMEM, tensor-map prefetch,
+// L2 prefetch hints) before pdl_wait(), which returns once the predecessor has
+// completed and its writes are visible; it then lets its own dependents launch
+// (pdl_trigger). Every kernel launched this way waits before it completes, so
+// all earlier work on the stream is complete once a kernel has passed its wait.
+// Outside such a launch both are no-ops. MLA_PDL=0 launches without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace mla
 

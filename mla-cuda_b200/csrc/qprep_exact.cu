@@ -188,6 +188,8 @@ __global__ void __launch_bounds__(1024) lat_norm_vec_kernel(
     const float* __restrict__ P1, int splits, const T* __restrict__ gain,
     OutT* __restrict__ q_lat, int64_t M, int64_t q_lora, float eps)
 {
+    pdl_wait();
+    pdl_trigger();
     constexpr int kMaxSplits = 16;                 // all split loads of a piece in flight at once
     const int64_t m = blockIdx.x;
     const int n4 = int(q_lora / 4);
@@ -640,6 +642,8 @@ namespace {
 
 __global__ void __launch_bounds__(256) cast_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst,
                                                         int64_t n4) {
+    pdl_wait();
+    pdl_trigger();
     for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(src) + i);
         __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
@@ -655,7 +659,7 @@ mla_status_t cast_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStre
     int64_t blocks = ceil_div(n4, 256);
     if (blocks > 8LL * sm_count()) blocks = 8LL * sm_count();
     if (blocks < 1) blocks = 1;
-    cast_bf16_kernel<<<unsigned(blocks), 256, 0, st>>>(src, dst, n4);
+    launch_pdl(cast_bf16_kernel, dim3(unsigned(blocks)), dim3(256), 0, st, src, dst, n4);
     return check_launch("bf16 cast");
 }
 
@@ -754,8 +758,9 @@ mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st) {
     {   // 2a-norm: fp32 arithmetic, bf16 latent for 2a2
         const unsigned threads = unsigned((a.q_lora / 4 + 31) / 32 * 32);
         if (p.split1 > 16) return set_error(MLA_ERR_UNSUPPORTED, "MLA: packed Q-prep split-K above 16");
-        lat_norm_vec_kernel<float, B16><<<unsigned(M), threads, 0, st>>>(
-            P1, p.split1, static_cast<const float*>(a.q_norm_w), q_lat, M, a.q_lora, float(a.eps));
+        launch_pdl(lat_norm_vec_kernel<float, B16>, dim3(unsigned(M)), dim3(threads), 0, st,
+                   static_cast<const float*>(P1), int(p.split1), static_cast<const float*>(a.q_norm_w), q_lat, M,
+                   int64_t(a.q_lora), float(a.eps));
         MLA_TRY(check_launch("q latent RMSNorm (2a-norm)"));
     }
 
@@ -773,7 +778,16 @@ mla_status_t qprep_packed(const QArgs& a, const void* packed, cudaStream_t st) {
     g2.B = pk + l.off_qb; g2.b_mn = true; g2.b_dims[0] = ncols; g2.b_dims[1] = a.q_lora; g2.b_dims[2] = 1;
     g2.b_ld[0] = ncols; g2.b_ld[1] = ncols * a.q_lora;
     g2.M = M; g2.N = ncols; g2.K = a.q_lora; g2.Z = 1; g2.spb = 1; g2.k_chunk = a.q_lora;
-    g2.C = nullptr; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.bn = 128; g2.err = err;
+    g2.C = nullptr; g2.c_is_t = false; g2.c_ldm = ncols; g2.c_ldz = M * ncols; g2.err = err;
+    // tile width: the fewest waves x columns per tile over the persistent grid (at
+    // N = 128 heads x 192 and 148 SMs, 192-column tiles fill one wave with a head each)
+    g2.bn = 128;
+    int64_t best = INT64_MAX;
+    for (const int bn : {128, 192, 256}) {
+        const int64_t tiles = ceil_div(ncols, int64_t(bn)) * ceil_div(M, int64_t(128));
+        const int64_t cost = ceil_div(tiles, int64_t(sm_count())) * bn;
+        if (cost < best) { best = cost; g2.bn = bn; }
+    }
     g2.rope_epi = &re;
     MLA_TRY(tc_gemm<B16>(g2, st));
 

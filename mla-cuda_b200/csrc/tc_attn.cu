@@ -330,6 +330,8 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
     tc_fence_after();
     cluster_sync();   // the peer's barriers exist before any remote arrive
     const uint32_t tmem = bars->tmem_base;
+    pdl_wait();       // the queries (and the cache) may come from the previous kernels
+    pdl_trigger();
 
     // Register split per warpgroup, set at the top of each role. setmaxnreg.inc
     // draws only on registers other warpgroups of this CTA released, so the
@@ -858,6 +860,8 @@ template <typename OutT>
 __global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups,
                                                       float* __restrict__ lse)
 {
+    pdl_wait();
+    pdl_trigger();
     const int64_t rowid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (rowid >= groups * kHeads) return;
@@ -1031,13 +1035,15 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         cfg.blockDim = dim3(kThreads, 1, 1);
         cfg.dynamicSmemBytes = smem;
         cfg.stream = st;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = 2;
         int* trace_host = nullptr;
         const size_t trace_bytes = size_t(2 * pl.nclusters) * 32 * sizeof(int);   // 32 words per CTA
         if (getenv("MLA_TC_TRACE")) {   // debug: progress words polled from the host while the kernel runs
@@ -1149,13 +1155,13 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
         const int64_t rows_total = pl.groups * kHeads;
         const unsigned cblocks = unsigned((rows_total * 32 + 255) / 256);
         if (a.v_dim % 32 != 0) {   // W_uv projection on CUDA cores from an fp32 context
-            combine_kernel<float><<<cblocks, 256, 0, st>>>(p, O_norm, pl.groups, a.lse);
+            launch_pdl(combine_kernel<float>, dim3(cblocks), dim3(256), 0, st, p, O_norm, int64_t(pl.groups), a.lse);
             MLA_TRY(check_launch("segment combine"));
             return attn_out_normalized<T>(a, O_norm, st);
         }
         // context in the storage dtype, then out[:, h] = ctx[:, h] @ W_uv[h]^T on the tensor cores
         T* ctx = reinterpret_cast<T*>(O_norm);
-        combine_kernel<T><<<cblocks, 256, 0, st>>>(p, ctx, pl.groups, a.lse);
+        launch_pdl(combine_kernel<T>, dim3(cblocks), dim3(256), 0, st, p, ctx, int64_t(pl.groups), a.lse);
         MLA_TRY(check_launch("segment combine"));
         TcGemm g{};
         g.A = ctx; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;

@@ -368,7 +368,9 @@ __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
 // (N tile fastest, then M tile, then launch index z). The shared-memory ring runs
 // on across units, and the accumulator is double-buffered in TMEM (2 x BN
 // columns), so the epilogue of one unit overlaps the loads and MMAs of the next.
-template <int BN> constexpr int pstages() { return BN == 256 ? 4 : 6; }
+template <int BN> constexpr int pstages() { return BN == 256 ? 4 : BN == 192 ? 5 : 6; }
+// TMEM allocations are powers of two: two 192-column accumulators take 512 columns
+template <int BN> constexpr uint32_t ptmem_cols() { return BN == 192 ? 512u : 2u * BN; }
 template <int BN> constexpr size_t psmem_bytes() {
     return 1024 + size_t(pstages<BN>()) * (a_bytes() + b_bytes<BN>()) + 256;
 }
@@ -386,7 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
     constexpr int BK = tc_gemm_bk<T>();
     constexpr int kInstK = 32 / int(sizeof(T));
     constexpr int kStage = a_bytes() + b_bytes<BN>();
-    constexpr uint32_t kTmemCols = 2u * BN;
+    constexpr uint32_t kTmemCols = ptmem_cols<BN>();
+    static_assert(kStage % 1024 == 0, "stages stay 1024-byte aligned (128B swizzle)");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStage);
@@ -423,14 +426,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();      // the operands and the output may belong to the previous kernel
+    pdl_trigger();
 
     if (warp == 0 && lane == 0) {
-        tma_prefetch_desc(&tmA);
-        tma_prefetch_desc(&tmB);
         int64_t it = 0;                      // k blocks issued so far (ring position)
         bool ok = true;
         for (int64_t u = blockIdx.x; u < U.total && ok; u += gridDim.x) {
@@ -616,7 +623,7 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
     const int64_t grid = U.total < sm_count() ? U.total : sm_count();
     GemmRopeEpilogue re{};
     if (g.rope_epi) re = *g.rope_epi;
-    kern<<<unsigned(grid), kThreads, smem, st>>>(ta, tb, r, U, re, g.rope_epi ? 1 : 0);
+    launch_pdl(kern, dim3(unsigned(grid)), dim3(kThreads), smem, st, ta, tb, r, U, re, g.rope_epi ? 1 : 0);
     return check_launch("tensor-core GEMM (persistent)");
 }
 
@@ -675,10 +682,12 @@ mla_status_t tc_gemm(const TcGemm& g, cudaStream_t st) {
                 g.N != e.heads * (e.nope + e.rope))
                 return set_error(MLA_ERR_UNSUPPORTED, "MLA: RoPE epilogue needs no split-K and 32-aligned parts");
             if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
+            if (g.bn == 192) return tcg::launch_persist<T, 192>(g, st);
             return tcg::launch_persist<T, 128>(g, st);
         }
         if (g.K2 == 0 && !g.rowmax && !tc_gemm_classic()) {
             if (g.bn == 256) return tcg::launch_persist<T, 256>(g, st);
+            if (g.bn == 192) return tcg::launch_persist<T, 192>(g, st);
             return tcg::launch_persist<T, 128>(g, st);
         }
         if (g.bn == 256) return tcg::launch<T, 256, false>(g, st);

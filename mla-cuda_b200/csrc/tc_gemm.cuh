@@ -42,7 +42,7 @@ struct TcGemm {
     int64_t M, N, K;
     int Z; int spb; int64_t k_chunk;
     void* C; bool c_is_t; int64_t c_ldm, c_ldz;
-    int bn;          // 128 or 256 output columns per CTA
+    int bn;          // 128 or 256 output columns per CTA (192: persistent form only)
     bool split3;
     // optional second operand pair, accumulated after A*B: C += A2*B2 over K2
     // (same layouts and boxes as A / B; spb must be 1)
