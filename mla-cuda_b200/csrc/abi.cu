@@ -104,8 +104,14 @@ auto dispatch(mla_dtype_t dt, F&& f) {
     }
 }
 
+// Tensor precision, and exact precision for 16-bit storage (tcgen05 kind::f16
+// products are exact in fp32; the kernel's exact variant keeps scores and
+// probabilities fp32-class), run the tensor-core attention where it covers the shape.
+bool exact16(mla_dtype_t dt, mla_precision_t prec) {
+    return prec == MLA_PREC_EXACT && (dt == MLA_DTYPE_BF16 || dt == MLA_DTYPE_F16);
+}
 bool use_tc_attention(mla_dtype_t dt, mla_precision_t prec, const AArgs& a) {
-    return prec == MLA_PREC_TENSOR && dt != MLA_DTYPE_F64 && tc_attention_supported(a);
+    return ((prec == MLA_PREC_TENSOR && dt != MLA_DTYPE_F64) || exact16(dt, prec)) && tc_attention_supported(a);
 }
 
 }  // namespace
@@ -276,7 +282,7 @@ static mla_status_t attention_impl(mla_dtype_t dtype, mla_precision_t precision,
     if (need > 0 && (!workspace || workspace_bytes < need))
         return set_error(MLA_ERR_WORKSPACE, "MLA mla_attention: workspace of %zu bytes needed, %zu given", need,
                          workspace ? workspace_bytes : size_t(0));
-    if (tc) return dispatch(dtype, [&](auto t) { return tc_attention<decltype(t)>(a, st); });
+    if (tc) return dispatch(dtype, [&](auto t) { return tc_attention<decltype(t)>(a, st, exact16(dtype, precision)); });
     return dispatch(dtype, [&](auto t) { return attn_exact<decltype(t)>(a, st); });
 }
 

@@ -432,20 +432,23 @@ mla_status_t launch_absorb(const typename Cfg::Acc* qn, const T* W, T* out, cons
 template <typename T> size_t qprep_tensor_workspace(const QArgs& a);
 template <typename T> mla_status_t qprep_tensor_impl(const QArgs& a, cudaStream_t st, bool split3);
 
-// fp32 storage: the exact path runs the tensor-core pipeline with 3xTF32 GEMMs
-// (fp32-class products, fp32 accumulation) wherever the shapes allow TMA tiles.
+// The exact path runs the tensor-core pipeline wherever the shapes allow TMA
+// tiles: fp32 storage with 3xTF32 GEMMs (fp32-class products, fp32
+// accumulation); 16-bit storage with kind::f16 GEMMs, whose 16-bit products are
+// exact in fp32 and accumulate in fp32 (the reference's policy for 16-bit
+// storage, with the same 16-bit intermediates). fp64 stays on CUDA cores.
 template <typename T>
-bool exact_uses_3xtf32(const QArgs& a) { return std::is_same<T, float>::value && qprep_tensor_supported<T>(a); }
+bool exact_uses_tc(const QArgs& a) { return !std::is_same<T, double>::value && qprep_tensor_supported<T>(a); }
 
 template <typename T>
 size_t qprep_exact_workspace(const QArgs& a) {
-    return exact_uses_3xtf32<T>(a) ? qprep_tensor_workspace<T>(a) : make_plan<T>(a).total;
+    return exact_uses_tc<T>(a) ? qprep_tensor_workspace<T>(a) : make_plan<T>(a).total;
 }
 
 template <typename T>
 mla_status_t qprep_exact(const QArgs& a, cudaStream_t st) {
     using Acc = acc_t<T>;
-    if (exact_uses_3xtf32<T>(a)) return qprep_tensor_impl<T>(a, st, true);
+    if (exact_uses_tc<T>(a)) return qprep_tensor_impl<T>(a, st, std::is_same<T, float>::value);
     const QPlan p = make_plan<T>(a);
     const int64_t M = a.batch * a.sq;
     const int64_t ncols = a.heads * (a.nope + a.rope);

@@ -91,7 +91,7 @@ constexpr int kXBufs = 2;                   // partial-score exchange buffers (f
 // (times log2(e)/scale) rounded to fp16, stored chunk-major (16-byte chunk e =
 // keys 8e..8e+7 of row r at (e*128 + r)*16), so that a warp's 32 rows write and
 // read 512 contiguous bytes per instruction
-constexpr int kXBytes = kHeads * NK * 2;
+constexpr int kXBytesF16 = kHeads * NK * 2;
 constexpr int kQRopeBytes = kHeads * kRopeHalf * 2;   // rope query slice: 128 rows of 64 B, 64B swizzle
 
 // TMEM columns: O half, kSBufs score / probability buffers, the query slice.
@@ -130,12 +130,27 @@ template <> struct Traits<__half> {
 // the slots; fp32 storage lands in staging, which the converter warps release
 // as soon as they have read it (so TMA keeps loads in flight), and is
 // converted into slots.
-template <typename T>
+// Kernel configuration. kExact (16-bit storage only) is the exact-precision
+// variant: the partial scores travel in fp32 (exchange buffers of 32 KB, one
+// slot fewer), and P is split into a 16-bit head and remainder, P = P_hi + P_lo,
+// both multiplied into V, so P.V carries the probabilities to about 2^-17
+// relative (the reference multiplies fp32 probabilities into the 16-bit cache).
+template <typename T, bool kExact> struct Cfg {
+    static constexpr bool kConvert = Traits<T>::kConvert;
+    static constexpr int kSlots = kExact ? 4 : Traits<T>::kSlots;
+    static constexpr int kStages = Traits<T>::kStages;
+    static constexpr uint32_t kFmt = Traits<T>::kFmt;
+    static constexpr int kXBytes = kExact ? kHeads * NK * 4 : kXBytesF16;
+};
+
+template <typename T, bool kExact = false>
 constexpr size_t smem_bytes() {
-    return 1024 /*align slack*/ + size_t(Traits<T>::kSlots) * kSlotBytes + size_t(Traits<T>::kStages) * kStgBytes +
-           kXBufs * size_t(kXBytes) + kQRopeBytes + 4096 /*barriers, row maxima, row sums*/;
+    using C = Cfg<T, kExact>;
+    return 1024 /*align slack*/ + size_t(C::kSlots) * kSlotBytes + size_t(C::kStages) * kStgBytes +
+           kXBufs * size_t(C::kXBytes) + kQRopeBytes + 4096 /*barriers, row maxima, row sums*/;
 }
-static_assert(smem_bytes<float>() <= 232448 && smem_bytes<__nv_bfloat16>() <= 232448, "shared memory budget");
+static_assert(smem_bytes<float>() <= 232448 && smem_bytes<__nv_bfloat16>() <= 232448 &&
+              smem_bytes<__nv_bfloat16, true>() <= 232448, "shared memory budget");
 
 struct Params {
     const void* qa;     // [B*Sq*H, 512]
@@ -267,17 +282,19 @@ __device__ __forceinline__ float2 unpack_x16(uint32_t v) {
     return __half22float2(h);
 }
 
-template <typename T>
+template <typename T, bool kExact>
 __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
     const __grid_constant__ CUtensorMap tm_ckv, const __grid_constant__ CUtensorMap tm_pe, const Params p)
 {
-    using Tr = Traits<T>;
+    using Tr = Cfg<T, kExact>;
+    static_assert(!kExact || !Traits<T>::kConvert, "the exact variant is for 16-bit storage");
+    constexpr int kXB = Tr::kXBytes;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* slots = smem;
     unsigned char* stg = slots + Tr::kSlots * kSlotBytes;
     float* xbuf = reinterpret_cast<float*>(stg + Tr::kStages * kStgBytes);
-    unsigned char* qrope = reinterpret_cast<unsigned char*>(xbuf) + kXBufs * kXBytes;
+    unsigned char* qrope = reinterpret_cast<unsigned char*>(xbuf) + kXBufs * kXB;
     Bars* bars = reinterpret_cast<Bars*>(qrope + kQRopeBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -314,7 +331,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
         // the softmax warp that consumed the buffer's previous tile)
         for (int i = 0; i < kXBufs; ++i)
             for (int w = 0; w < 4; ++w) {
-                mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(32 * NK * 2));
+                mbar_arrive_expect_tx(&bars->x_full[i][w], uint32_t(kXB / 4));   // one warp's 32 rows
                 mbar_arrive_expect_tx(&bars->x_free[i][w], 4u);   // the signal freeing the buffer for tile i+2
             }
         bars->abort = 0;
@@ -407,6 +424,12 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     for (int k = 0; k < NK / 16; ++k)
                         mma_ts(tmem + kTmemO, p_tmem + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4), idesc_o,
                                (first && k == 0) ? 0u : 1u);
+                    if constexpr (kExact) {   // + P_lo . V (P_lo in columns NK/2.. of the buffer)
+#pragma unroll
+                        for (int k = 0; k < NK / 16; ++k)
+                            mma_ts(tmem + kTmemO, p_tmem + NK / 2 + k * 8, vd0 + uint64_t((k * 16 * 128) >> 4),
+                                   idesc_o, 1u);
+                    }
                     mma_commit(&bars->bf_empty[sl]);
                     mma_commit(&bars->o_done[sb]);
                     MLA_TL(1, i);
@@ -469,7 +492,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
             const uint32_t lane_off = uint32_t(wq * 32) << 16;
             const float c = p.c_log2;
             // peer addresses of my exchange row (chunk 0) and of my warp's exchange
-            // barriers (buffer 0; buffer b is at +b*kXBytes / +b*4*8 bytes)
+            // barriers (buffer 0; buffer b is at +b*kXB / +b*4*8 bytes)
             const uint32_t xpeer0 = map_peer(xbuf + row * 4, peer);
             const uint32_t xbar_peer0 = map_peer(&bars->x_full[0][wq], peer);
             TileIter itp = locate(p, t_begin);
@@ -542,21 +565,32 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                                                        ERR_TIMEOUT_BASE + 7, /*cluster_scope=*/true))))
                     break;
                 if (lane == 0 && i >= kXBufs && i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_free[xb][wq], 4u);
-                // st.async pushes my partial (log2 units, fp16), counted on the peer's barrier
+                // st.async pushes my partial (log2 units in fp16; raw fp32 in the exact
+                // variant), counted on the peer's barrier
 #pragma unroll
                 for (int h = 0; h < NK / 32; ++h) {   // 32 keys at a time
                     uint32_t sr[32];
                     tmem_ld32(tmem + lane_off + kTmemS + sb * NK + h * 32, sr);
                     tmem_ld_wait();
+                    if constexpr (kExact) {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {      // chunk h*4+e: keys 32h+8e .. +7
-                        uint32_t w[4];
+                        for (int e = 0; e < 8; ++e)    // chunk h*8+e: keys 32h+4e .. +3
+                            st_async_v4(xpeer0 + uint32_t(xb) * kXB + uint32_t(h * 8 + e) * (kHeads * 16),
+                                        __uint_as_float(sr[4 * e]), __uint_as_float(sr[4 * e + 1]),
+                                        __uint_as_float(sr[4 * e + 2]), __uint_as_float(sr[4 * e + 3]),
+                                        xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
+                    } else {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q)
-                            w[q] = pack_x16(__uint_as_float(sr[8 * e + 2 * q]), __uint_as_float(sr[8 * e + 2 * q + 1]), c);
-                        st_async_v4(xpeer0 + uint32_t(xb) * kXBytes + uint32_t(h * 4 + e) * (kHeads * 16),
-                                    __uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]),
-                                    __uint_as_float(w[3]), xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
+                        for (int e = 0; e < 4; ++e) {  // chunk h*4+e: keys 32h+8e .. +7
+                            uint32_t w[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                w[q] = pack_x16(__uint_as_float(sr[8 * e + 2 * q]), __uint_as_float(sr[8 * e + 2 * q + 1]),
+                                                c);
+                            st_async_v4(xpeer0 + uint32_t(xb) * kXB + uint32_t(h * 4 + e) * (kHeads * 16),
+                                        __uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]),
+                                        __uint_as_float(w[3]), xbar_peer0 + uint32_t(xb) * uint32_t(4 * 8));
+                        }
                     }
                 }
                 tc_fence_before();
@@ -618,22 +652,41 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 {
                     uint32_t sr[32];
                     tmem_ld32(tmem + lane_off + kTmemS + sb * NK + hk * 32, sr);
-                    const uint4* xr = reinterpret_cast<const uint4*>(
-                        reinterpret_cast<const unsigned char*>(xbuf) + xb * kXBytes + (hk * 4 * kHeads + row) * 16);
-                    uint4 pv[4];
+                    if constexpr (kExact) {
+                        // fp32 chunks hk*8+e: the two halves add the same two values in
+                        // either order, so both CTAs hold the same sums
+                        const float4* xr = reinterpret_cast<const float4*>(
+                            reinterpret_cast<const unsigned char*>(xbuf) + xb * kXB + (hk * 8 * kHeads + row) * 16);
+                        float4 pv[8];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) pv[e] = xr[e * kHeads];
-                    tmem_ld_wait();
+                        for (int e = 0; e < 8; ++e) pv[e] = xr[e * kHeads];
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const uint32_t pw[4] = {pv[e].x, pv[e].y, pv[e].z, pv[e].w};
+                        for (int e = 0; e < 8; ++e) {
+                            s[4 * e] = (__uint_as_float(sr[4 * e]) + pv[e].x) * c;
+                            s[4 * e + 1] = (__uint_as_float(sr[4 * e + 1]) + pv[e].y) * c;
+                            s[4 * e + 2] = (__uint_as_float(sr[4 * e + 2]) + pv[e].z) * c;
+                            s[4 * e + 3] = (__uint_as_float(sr[4 * e + 3]) + pv[e].w) * c;
+                        }
+                    } else {
+                        const uint4* xr = reinterpret_cast<const uint4*>(
+                            reinterpret_cast<const unsigned char*>(xbuf) + xb * kXB + (hk * 4 * kHeads + row) * 16);
+                        uint4 pv[4];
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            const int k = 8 * e + 2 * q;
-                            const float2 mine = unpack_x16(pack_x16(__uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), c));
-                            const float2 peer = unpack_x16(pw[q]);
-                            s[k] = mine.x + peer.x;
-                            s[k + 1] = mine.y + peer.y;
+                        for (int e = 0; e < 4; ++e) pv[e] = xr[e * kHeads];
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t pw[4] = {pv[e].x, pv[e].y, pv[e].z, pv[e].w};
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int k = 8 * e + 2 * q;
+                                const float2 mine =
+                                    unpack_x16(pack_x16(__uint_as_float(sr[k]), __uint_as_float(sr[k + 1]), c));
+                                const float2 peer = unpack_x16(pw[q]);
+                                s[k] = mine.x + peer.x;
+                                s[k + 1] = mine.y + peer.y;
+                            }
                         }
                     }
                 }
@@ -663,7 +716,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 // a maximum that depends on every value it read): announce the bytes of
                 // the buffer's next tile (i+2) and free it for the peer's push.
                 if (hk == 0 && lane == 0) {
-                    if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(32 * NK * 2));
+                    if (i + kXBufs < n) mbar_arrive_expect_tx(&bars->x_full[xb][wq], uint32_t(kXB / 4));
                     st_async_b32(sink_peer0 + uint32_t(xb) * 16u, mt, xfree_peer0 + uint32_t(xb) * 32u);
                 }
                 if (first) {
@@ -695,7 +748,8 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 }
                 MLA_PROF(wacc[21] += clock64() - t_f1; const long long t_f2 = clock64();)
                 const float mc = m_run;
-                uint32_t pk[16];
+                uint32_t pk[16];                  // P (16-bit pairs); the exact variant's P_hi
+                uint32_t pl[kExact ? 16 : 1];     // the exact variant's P_lo = P - P_hi
                 float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
@@ -705,8 +759,16 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     if constexpr (Tr::kFmt == 0) {
                         __half2 h2 = __floats2half2_rn(p0, p1);
                         pk[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+                        if constexpr (kExact) {
+                            const float2 f = __half22float2(h2);
+                            __half2 l2 = __floats2half2_rn(p0 - f.x, p1 - f.y);
+                            pl[e / 2] = *reinterpret_cast<uint32_t*>(&l2);
+                        }
                     } else {
                         pk[e / 2] = pack_bf16(p0, p1);
+                        if constexpr (kExact)
+                            pl[e / 2] = pack_bf16(p0 - __uint_as_float(pk[e / 2] << 16),
+                                                  p1 - __uint_as_float(pk[e / 2] & 0xffff0000u));
                     }
                 }
                 l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
@@ -719,6 +781,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     break;
                 __syncwarp();
                 tmem_st16(tmem + lane_off + kTmemS + sb * NK + hk * 16, pk);
+                if constexpr (kExact) tmem_st16(tmem + lane_off + kTmemS + sb * NK + NK / 2 + hk * 16, pl);
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[sb]);
@@ -987,7 +1050,7 @@ size_t tc_attention_workspace(const AArgs& a) {
 }
 
 template <typename T>
-mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
+mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
     if constexpr (std::is_same<T, double>::value) {
         return set_error(MLA_ERR_UNSUPPORTED, "MLA: tensor-core attention has no fp64 variant");
     } else {
@@ -1020,7 +1083,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
             !make_map<T>(&tm_pe, a.pe_cache, rows, kRope, kRopeHalf, box_rows, direct ? 64 : 0))
             return set_error(MLA_ERR_CUDA, "MLA: cuTensorMapEncodeTiled failed (alignment of c_kv / pe_cache?)");
 
-        auto kern = mla_decode_tc_kernel<T>;
+        constexpr bool k16 = !std::is_same<T, float>::value;
+        if (exact && !k16) return set_error(MLA_ERR_UNSUPPORTED, "MLA: the exact tensor-core attention is for 16-bit storage");
+        auto kern = (k16 && exact) ? mla_decode_tc_kernel<T, k16> : mla_decode_tc_kernel<T, false>;
         cudaFuncAttributes fa{};
         if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess || fa.numRegs != kLaunchRegs ||
             fa.maxThreadsPerBlock < kThreads)
@@ -1028,7 +1093,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st) {
                              "MLA: decode kernel compiled with %d registers per thread (expected %d; max threads %d): "
                              "its register split would not fit, not launching", fa.numRegs, kLaunchRegs,
                              fa.maxThreadsPerBlock);
-        const size_t smem = smem_bytes<T>();
+        const size_t smem = (k16 && exact) ? smem_bytes<T, k16>() : smem_bytes<T, false>();
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(unsigned(2 * pl.nclusters), 1, 1);
@@ -1179,9 +1244,9 @@ template size_t tc_attention_workspace<float>(const AArgs&);
 template size_t tc_attention_workspace<double>(const AArgs&);
 template size_t tc_attention_workspace<__half>(const AArgs&);
 template size_t tc_attention_workspace<__nv_bfloat16>(const AArgs&);
-template mla_status_t tc_attention<float>(const AArgs&, cudaStream_t);
-template mla_status_t tc_attention<double>(const AArgs&, cudaStream_t);
-template mla_status_t tc_attention<__half>(const AArgs&, cudaStream_t);
-template mla_status_t tc_attention<__nv_bfloat16>(const AArgs&, cudaStream_t);
+template mla_status_t tc_attention<float>(const AArgs&, cudaStream_t, bool);
+template mla_status_t tc_attention<double>(const AArgs&, cudaStream_t, bool);
+template mla_status_t tc_attention<__half>(const AArgs&, cudaStream_t, bool);
+template mla_status_t tc_attention<__nv_bfloat16>(const AArgs&, cudaStream_t, bool);
 
 }  // namespace mla
