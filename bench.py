@@ -63,8 +63,8 @@ def parse():
                     help="launch the timed layer forwards one by one instead of replaying a CUDA graph of one")
     ap.add_argument("--no-parity", action="store_true", help="skip the sampled-sequence parity check")
     ap.add_argument("--weights", default="packed", choices=["packed", "plain"],
-                    help="tensor precision, fp32 storage: Q-prep from weights packed once to bf16 (default) or "
-                         "from the fp32 weights on every call")
+                    help="tensor precision, fp32 storage: W_q_a / W_q_b / W_uk / W_uv packed once to bf16 "
+                         "(default) or the fp32 weights on every call")
     ap.add_argument("--no-key-shard-c2", action="store_true",
                     help="with --gpus N > 1, skip the extra key-sharded c2 measurement")
     ap.add_argument("--qprep", default="redundant", choices=["heads", "redundant"],
@@ -174,7 +174,7 @@ class ClockSampler:
 
 
 KEY_SHARDED = {"on": False, "heads": False}
-PACKED = {"w": None}   # PackedQWeights when the step uses pre-packed Q-prep weights
+PACKED = {"w": None, "uv": None}   # PackedQWeights / PackedUVWeights when the step uses pre-packed weights
 
 # DRAM bytes per launch of the decode kernel, from the ncu capture named below
 # (dram__bytes_read.sum + dram__bytes_write.sum), keyed by (config, precision,
@@ -201,6 +201,9 @@ def run_forward(mcc, t, w, precision):
         from mla_custom_cuda import sharding
         return sharding.sk_sharded_attention(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,
                                              precision=precision), qa, qr
+    if PACKED["uv"] is not None and precision == "tensor":
+        return mcc.mla_attention_packed(qa, qr, t["c_kv"], t["pe_cache"], PACKED["uv"], w.scale,
+                                        causal=w.causal), qa, qr
     return mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale, causal=w.causal,
                                 precision=precision), qa, qr
 
@@ -472,6 +475,7 @@ def main_ours(args):
             and not KEY_SHARDED["heads"]):
         # weight-load time, outside every timed region: one bf16 copy of W_q_a, W_q_b, W_uk
         PACKED["w"] = mcc.pack_q_weights(t["W_q_a"], t["W_q_b"], t["W_uk"], w.nope, w.rope)
+        PACKED["uv"] = mcc.pack_uv_weights(t["W_uv"])
         torch.cuda.synchronize()
 
     def barrier():
@@ -556,6 +560,9 @@ def main_ours(args):
         if KEY_SHARDED["on"]:
             att_fn = lambda: mcc.mla_attention_partial(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,  # noqa
                                                        precision=prec)
+        elif prec == "tensor" and PACKED["uv"] is not None:
+            att_fn = lambda: mcc.mla_attention_packed(qa, qr, t["c_kv"], t["pe_cache"], PACKED["uv"], w.scale,  # noqa
+                                                      causal=w.causal)
         else:
             att_fn = lambda: mcc.mla_attention_ex(qa, qr, t["c_kv"], t["pe_cache"], t["W_uv"], w.scale,  # noqa
                                                   causal=w.causal, precision=prec)
@@ -744,8 +751,8 @@ def main_ours(args):
             "precision": precision,
             "launch": ("CUDA graph of one layer forward (q_absorbed + mla_attention), replayed per step"
                        if use_graph else "eager calls per step")
-                      + ("; Q-prep from weights packed once to bf16 at load (q_absorbed_packed)"
-                         if PACKED["w"] is not None else "")
+                      + ("; W_q_a / W_q_b / W_uk / W_uv packed once to bf16 at load (q_absorbed_packed, "
+                         "mla_attention_packed)" if PACKED["w"] is not None else "")
                       + (", Q-prep head-sharded + all-gather of q" if KEY_SHARDED["heads"] else ""),
             "stages": stages,
             "roofline": {"bound": "hbm",

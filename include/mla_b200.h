@@ -180,6 +180,35 @@ MLA_API mla_status_t mla_attention(
     void* out,
     void* workspace, size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------- pre-packed W_uv ---------
+ * Beside the drop-in, like mla_pack_q_weights. For fp32 storage in tensor
+ * precision, W_uv [heads, v_dim, kv_rank] can be converted once to bf16 (a
+ * buffer of mla_pack_uv_weights_size() bytes, same layout); then
+ * mla_attention_packed_uv runs mla_attention with MLA_PREC_TENSOR, keeping the
+ * normalised context in bf16 and projecting it with the bf16 W_uv (kind::f16,
+ * fp32 accumulation, fp32 output): the 3d step streams half the bytes.
+ * Operands, workspace (mla_attention_workspace_size with MLA_PREC_TENSOR) and
+ * output are those of mla_attention; dtype must be MLA_DTYPE_F32 and the shape
+ * one the tensor-core attention covers (heads 128, kv_rank 512, rope 64, v_dim
+ * a multiple of 32), else MLA_ERR_UNSUPPORTED.
+ */
+MLA_API mla_status_t mla_pack_uv_weights_size(
+    mla_dtype_t dtype, int64_t heads, int64_t v_dim, int64_t kv_rank, size_t* bytes);
+
+MLA_API mla_status_t mla_pack_uv_weights(
+    mla_dtype_t dtype, const void* W_uv, int64_t heads, int64_t v_dim, int64_t kv_rank,
+    void* packed, size_t packed_bytes, void* stream);
+
+MLA_API mla_status_t mla_attention_packed_uv(
+    mla_dtype_t dtype,
+    const void* q_absorbed, const void* q_rope,
+    const void* c_kv, const void* pe_cache, const void* W_uv_packed,
+    int64_t batch, int64_t sq, int64_t sk, int64_t heads,
+    int64_t kv_rank, int64_t rope, int64_t v_dim,
+    double scale, int causal,
+    void* out,
+    void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------- KV-cache write --
  * The step upstream of the decode read. The reference has no kernel for it
  * (its caches are inputs; the write is only mentioned,

@@ -258,7 +258,8 @@ mla_status_t mla_attention_workspace_size(mla_dtype_t dtype, mla_precision_t pre
 static mla_status_t attention_impl(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed, const void* q_rope,
                            const void* c_kv, const void* pe_cache, const void* W_uv, int64_t batch, int64_t sq,
                            int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim, double scale,
-                           int causal, void* out, float* lse, void* workspace, size_t workspace_bytes, void* stream) {
+                           int causal, void* out, float* lse, void* workspace, size_t workspace_bytes, void* stream,
+                           const void* W_uv_bf16 = nullptr) {
     MLA_TRY(validate_a(dtype, precision, batch, sq, sk, heads, kv_rank, rope, v_dim, causal));
     if (batch * sq == 0) return MLA_OK;
     if (!out || !W_uv || !q_absorbed) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: null pointer");
@@ -276,6 +277,7 @@ static mla_status_t attention_impl(mla_dtype_t dtype, mla_precision_t precision,
     if (scale == 0.0) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention: scale must be non-zero");
     AArgs a{q_absorbed, q_rope, c_kv, pe_cache, W_uv, batch, sq, sk, heads, kv_rank, rope, v_dim,
             scale, causal, out, workspace, workspace_bytes, lse};
+    a.W_uv_bf16 = W_uv_bf16;
     const bool tc = use_tc_attention(dtype, precision, a);
     const size_t need = tc ? dispatch(dtype, [&](auto t) { return tc_attention_workspace<decltype(t)>(a); })
                            : dispatch(dtype, [&](auto t) { return attn_exact_workspace<decltype(t)>(a); });
@@ -294,6 +296,49 @@ mla_status_t mla_attention(mla_dtype_t dtype, mla_precision_t precision, const v
                            int causal, void* out, void* workspace, size_t workspace_bytes, void* stream) {
     return attention_impl(dtype, precision, q_absorbed, q_rope, c_kv, pe_cache, W_uv, batch, sq, sk, heads, kv_rank,
                           rope, v_dim, scale, causal, out, nullptr, workspace, workspace_bytes, stream);
+}
+
+mla_status_t mla_pack_uv_weights_size(mla_dtype_t dtype, int64_t heads, int64_t v_dim, int64_t kv_rank, size_t* bytes) {
+    if (dtype != MLA_DTYPE_F32)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA: W_uv packing is for fp32 storage (16-bit weights are used as is)");
+    if (!bytes) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA: bytes must not be NULL");
+    if (heads <= 0 || v_dim <= 0 || kv_rank <= 0)
+        return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA pack_uv_weights: sizes must be positive");
+    *bytes = size_t(heads * v_dim * kv_rank) * 2;
+    return MLA_OK;
+}
+
+mla_status_t mla_pack_uv_weights(mla_dtype_t dtype, const void* W_uv, int64_t heads, int64_t v_dim, int64_t kv_rank,
+                                 void* packed, size_t packed_bytes, void* stream) {
+    size_t need = 0;
+    MLA_TRY(mla_pack_uv_weights_size(dtype, heads, v_dim, kv_rank, &need));
+    if (!W_uv || !packed) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA pack_uv_weights: null pointer");
+    if (packed_bytes < need)
+        return set_error(MLA_ERR_WORKSPACE, "MLA pack_uv_weights: %zu bytes needed, %zu given", need, packed_bytes);
+    if ((heads * v_dim * kv_rank) % 4 != 0 || reinterpret_cast<uintptr_t>(W_uv) % 16 != 0 ||
+        reinterpret_cast<uintptr_t>(packed) % 16 != 0)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA pack_uv_weights: needs a multiple of 4 elements, 16-byte aligned");
+    return cast_to_bf16(static_cast<const float*>(W_uv), static_cast<__nv_bfloat16*>(packed), heads * v_dim * kv_rank,
+                        static_cast<cudaStream_t>(stream));
+}
+
+mla_status_t mla_attention_packed_uv(mla_dtype_t dtype, const void* q_absorbed, const void* q_rope, const void* c_kv,
+                                     const void* pe_cache, const void* W_uv_packed, int64_t batch, int64_t sq,
+                                     int64_t sk, int64_t heads, int64_t kv_rank, int64_t rope, int64_t v_dim,
+                                     double scale, int causal, void* out, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+    if (dtype != MLA_DTYPE_F32)
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA mla_attention_packed_uv: fp32 storage only");
+    AArgs a{};
+    a.batch = batch; a.sq = sq; a.sk = sk; a.heads = heads; a.kv_rank = kv_rank; a.rope = rope; a.v_dim = v_dim;
+    a.causal = causal;
+    if (batch * sq > 0 && sk > 0 && (!tc_attention_supported(a) || v_dim % 32 != 0))
+        return set_error(MLA_ERR_UNSUPPORTED, "MLA mla_attention_packed_uv: shape not covered by the tensor-core "
+                                              "attention (heads 128, kv_rank 512, rope 64, v_dim a multiple of 32)");
+    if (!W_uv_packed) return set_error(MLA_ERR_INVALID_ARGUMENT, "MLA mla_attention_packed_uv: null W_uv_packed");
+    return attention_impl(dtype, MLA_PREC_TENSOR, q_absorbed, q_rope, c_kv, pe_cache, W_uv_packed, batch, sq, sk,
+                          heads, kv_rank, rope, v_dim, scale, causal, out, nullptr, workspace, workspace_bytes, stream,
+                          W_uv_packed);
 }
 
 mla_status_t mla_attention_partial(mla_dtype_t dtype, mla_precision_t precision, const void* q_absorbed,

@@ -25,7 +25,11 @@ struct AArgs {
     void* out;
     void* workspace; size_t workspace_bytes;
     float* lse;   // optional [B*Sq*H]: natural-log sum of exp(score) per row (partial attention)
+    const void* W_uv_bf16;   // optional (fp32 storage, tensor precision): bf16 W_uv; bf16 context for 3d
 };
+
+// fp32 -> bf16 copy of n elements (n a multiple of 4), 16-byte aligned buffers
+mla_status_t cast_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t st);
 
 template <typename T> size_t qprep_exact_workspace(const QArgs& a);
 template <typename T> mla_status_t qprep_exact(const QArgs& a, cudaStream_t st);

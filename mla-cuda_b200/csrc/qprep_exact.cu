@@ -710,6 +710,10 @@ QPPlan make_pplan(const QArgs& a) {
 
 }  // namespace
 
+mla_status_t cast_to_bf16(const float* src, __nv_bfloat16* dst, int64_t n, cudaStream_t st) {
+    return cast_bf16(src, dst, n, st);
+}
+
 bool qprep_packed_supported(const QArgs& a) {
     const int64_t ncols = a.heads * (a.nope + a.rope);
     return a.q_lora % 32 == 0 && ncols % 32 == 0 && a.kv_rank % 32 == 0 && a.hidden % 8 == 0 && a.q_lora % 8 == 0 &&

@@ -1224,6 +1224,23 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
             MLA_TRY(check_launch("segment combine"));
             return attn_out_normalized<T>(a, O_norm, st);
         }
+        if constexpr (std::is_same<T, float>::value) {
+            if (a.W_uv_bf16) {   // pre-packed W_uv: bf16 context, kind::f16 projection, fp32 output
+                __nv_bfloat16* ctx16 = reinterpret_cast<__nv_bfloat16*>(O_norm);
+                launch_pdl(combine_kernel<__nv_bfloat16>, dim3(cblocks), dim3(256), 0, st, p, ctx16,
+                           int64_t(pl.groups), a.lse);
+                MLA_TRY(check_launch("segment combine"));
+                TcGemm g{};
+                g.A = ctx16; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;
+                g.a_ld[0] = kRank; g.a_ld[1] = int64_t(kHeads) * kRank;
+                g.B = a.W_uv_bf16; g.b_mn = false; g.b_dims[0] = kRank; g.b_dims[1] = a.v_dim; g.b_dims[2] = kHeads;
+                g.b_ld[0] = kRank; g.b_ld[1] = a.v_dim * kRank;
+                g.M = pl.groups; g.N = a.v_dim; g.K = kRank; g.Z = kHeads; g.spb = 1; g.k_chunk = kRank;
+                g.C = a.out; g.c_is_t = false; g.c_ldm = int64_t(kHeads) * a.v_dim; g.c_ldz = a.v_dim;
+                g.bn = a.v_dim % 256 == 0 ? 256 : 128; g.err = p.err;
+                return tc_gemm<__nv_bfloat16>(g, st);
+            }
+        }
         // context in the storage dtype, then out[:, h] = ctx[:, h] @ W_uv[h]^T on the tensor cores
         T* ctx = reinterpret_cast<T*>(O_norm);
         launch_pdl(combine_kernel<T>, dim3(cblocks), dim3(256), 0, st, p, ctx, int64_t(pl.groups), a.lse);

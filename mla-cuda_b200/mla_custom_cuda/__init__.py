@@ -46,6 +46,7 @@ __all__ = [
     "set_precision", "get_precision", "library_path", "abi_version",
     "device_status", "clear_device_status", "check_device", "set_wait_limit_ns", "wait_selftest",
     "kernel_timing", "kv_cache_write", "pack_q_weights", "q_absorbed_packed", "PackedQWeights",
+    "pack_uv_weights", "mla_attention_packed", "PackedUVWeights",
 ]
 
 _LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libmla_b200.so"
@@ -108,6 +109,13 @@ def _load() -> ctypes.CDLL:
     lib.mla_kv_cache_write.restype = ctypes.c_int
     lib.mla_kv_cache_write.argtypes = ([ctypes.c_int, ctypes.c_int] + [_c_vp] * 5 + [_c_i64] * 6
                                        + [ctypes.c_double, _c_vp, _c_vp, _c_vp, _c_size, _c_vp])
+    lib.mla_pack_uv_weights_size.restype = ctypes.c_int
+    lib.mla_pack_uv_weights_size.argtypes = [ctypes.c_int] + [_c_i64] * 3 + [ctypes.POINTER(_c_size)]
+    lib.mla_pack_uv_weights.restype = ctypes.c_int
+    lib.mla_pack_uv_weights.argtypes = [ctypes.c_int, _c_vp] + [_c_i64] * 3 + [_c_vp, _c_size, _c_vp]
+    lib.mla_attention_packed_uv.restype = ctypes.c_int
+    lib.mla_attention_packed_uv.argtypes = ([ctypes.c_int] + [_c_vp] * 5 + [_c_i64] * 7
+                                            + [ctypes.c_double, ctypes.c_int, _c_vp, _c_vp, _c_size, _c_vp])
     lib.mla_timing_enable.restype = ctypes.c_int
     lib.mla_timing_enable.argtypes = [ctypes.c_int]
     lib.mla_timing_read.restype = ctypes.c_int
@@ -470,6 +478,72 @@ def mla_attention_ex(q_absorbed, q_rope, c_kv, pe_cache, W_uv, scale: float, cau
                                 wv.data_ptr(), B, Sq, Sk, H, R, D, V, float(scale), int(bool(causal)),
                                 out.data_ptr(), ws.data_ptr(), ws.numel(), stream)
     _raise_status(st, "mla_attention")
+    _after_call(device)
+    return out
+
+
+class PackedUVWeights:
+    """W_uv [H, v_dim, kv_rank] converted once to bf16, for mla_attention_packed."""
+
+    def __init__(self, buf: torch.Tensor, heads: int, v_dim: int, kv_rank: int):
+        self.buf, self.heads, self.v_dim, self.kv_rank = buf, heads, v_dim, kv_rank
+
+    @property
+    def device(self):
+        return self.buf.device
+
+
+def pack_uv_weights(W_uv) -> PackedUVWeights:
+    """One-time bf16 packing of the fp32 W_uv (at weight-load time). The
+    reference passes W_uv on every call and converts nothing
+    (exhaustive_benchmark_suite.py:261-265)."""
+    dtype, device = _float_operands([("W_uv", W_uv)])
+    _check(dtype == torch.float32, "pack_uv_weights: fp32 W_uv only (16-bit weights are used as they are)")
+    _check(W_uv.dim() == 3, f"W_uv must be [H,v_dim,kv_rank] (got {tuple(W_uv.shape)})")
+    H, V, R = W_uv.shape
+    nbytes = _c_size(0)
+    _raise_status(_lib.mla_pack_uv_weights_size(0, H, V, R, ctypes.byref(nbytes)), "pack_uv_weights")
+    buf = torch.empty(int(nbytes.value) // 2, dtype=torch.bfloat16, device=device)
+    wv = W_uv.contiguous()
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_pack_uv_weights(0, wv.data_ptr(), H, V, R, buf.data_ptr(), int(nbytes.value),
+                                               _stream_of(device)), "pack_uv_weights")
+    return PackedUVWeights(buf, H, V, R)
+
+
+def mla_attention_packed(q_absorbed, q_rope, c_kv, pe_cache, packed: PackedUVWeights, scale: float,
+                         causal: bool = False) -> torch.Tensor:
+    """mla_attention at tensor precision (fp32 storage) with a W_uv packed by
+    pack_uv_weights: the normalised context stays in bf16 and is projected with
+    the bf16 W_uv; returns fp32 [B,Sq,H,v_dim]."""
+    dtype, device = _float_operands([("q_absorbed", q_absorbed), ("q_rope", q_rope), ("c_kv", c_kv),
+                                     ("pe_cache", pe_cache)])
+    _check(dtype == torch.float32, "mla_attention_packed: fp32 storage")
+    _check(isinstance(packed, PackedUVWeights) and packed.device == device,
+           "packed must be a PackedUVWeights on the operands' device")
+    _check(q_absorbed.dim() == 4, f"q_absorbed must be [B,Sq,H,kv_rank] (got {tuple(q_absorbed.shape)})")
+    B, Sq, H, R = q_absorbed.shape
+    _check(H == packed.heads and R == packed.kv_rank, "packed W_uv does not match q_absorbed's heads / kv_rank")
+    _check(q_rope.dim() == 4 and tuple(q_rope.shape[:3]) == (B, Sq, H),
+           f"q_rope must be [B,Sq,H,rope] (got {tuple(q_rope.shape)})")
+    D = q_rope.shape[3]
+    _check(c_kv.dim() == 3 and c_kv.shape[0] == B and c_kv.shape[2] == R,
+           f"c_kv must be [B,Sk,kv_rank] (got {tuple(c_kv.shape)})")
+    Sk = c_kv.shape[1]
+    _check(tuple(pe_cache.shape) == (B, Sk, D), f"pe_cache must be [B,Sk,rope] (got {tuple(pe_cache.shape)})")
+    V = packed.v_dim
+    qa, qr, ck, pe = (t.contiguous() for t in (q_absorbed, q_rope, c_kv, pe_cache))
+    out = torch.empty((B, Sq, H, V), dtype=dtype, device=device)
+    nbytes = _c_size(0)
+    with torch.cuda.device(device):
+        _raise_status(_lib.mla_attention_workspace_size(0, 1, B, Sq, Sk, H, R, D, V, int(bool(causal)),
+                                                        ctypes.byref(nbytes)), "mla_attention_packed")
+        ws = torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=device)
+        st = _lib.mla_attention_packed_uv(0, qa.data_ptr(), qr.data_ptr(), ck.data_ptr(), pe.data_ptr(),
+                                          packed.buf.data_ptr(), B, Sq, Sk, H, R, D, V, float(scale),
+                                          int(bool(causal)), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                          _stream_of(device))
+    _raise_status(st, "mla_attention_packed")
     _after_call(device)
     return out
 

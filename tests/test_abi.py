@@ -146,3 +146,28 @@ def test_status_strings_cover_every_code(lib):
     lib.mla_status_string.restype = ctypes.c_char_p
     names = [lib.mla_status_string(c).decode() for c in range(6)]
     assert names[5] == "device-side failure" and len(set(names)) == 6
+
+
+def test_pack_uv_weights_and_packed_attention_validation(lib):
+    f = lib.mla_pack_uv_weights_size
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_int] + [ctypes.c_int64] * 3 + [ctypes.POINTER(ctypes.c_size_t)]
+    n = _size_t()
+    assert f(0, 128, 128, 512, ctypes.byref(n)) == 0 and n.value == 128 * 128 * 512 * 2   # one bf16 copy
+    assert f(3, 128, 128, 512, ctypes.byref(n)) == 2      # bf16 storage: MLA_ERR_UNSUPPORTED
+    assert f(0, 0, 128, 512, ctypes.byref(n)) == 1        # empty: invalid argument
+    g = lib.mla_pack_uv_weights
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.c_int, ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_size_t,
+                                                                           ctypes.c_void_p]
+    assert g(0, None, 128, 128, 512, None, 0, None) == 1  # null pointers
+    a = lib.mla_attention_packed_uv
+    a.restype = ctypes.c_int
+    a.argtypes = ([ctypes.c_int] + [ctypes.c_void_p] * 5 + [ctypes.c_int64] * 7
+                  + [ctypes.c_double, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p])
+    args = [None] * 5 + [4, 1, 4989, 128, 512, 64, 128, 13.856, 0, None, None, 0, None]
+    assert a(2, *args) == 2                                # fp16 storage: unsupported
+    bad = list(args)
+    bad[8] = 256                                           # kv_rank 256: not a tensor-core shape
+    assert a(0, *bad) == 2
+    assert a(0, *args) == 1                                # covered shape, null W_uv_packed: invalid argument

@@ -181,3 +181,33 @@ def test_packed_q_absorbed_vs_oracle(mcc, B, Sq):
     qa2, qr2 = mcc.q_absorbed_ex(g["x"], g["W_q_a"], g["q_norm_w"], g["W_q_b"], g["W_uk"], g["positions"],
                                  mc.NOPE, mc.ROPE, mc.EPS, precision="tensor")
     assert rel_l2(qa, qa2) < TOL
+
+
+@pytest.mark.parametrize("fname", ATTN_FILES)
+def test_packed_uv_attention_vs_golden(mcc, fname):
+    """Attention with W_uv packed to bf16 (bf16 context, kind::f16 projection,
+    fp32 output) against the reference goldens, and against the unpacked
+    tensor-precision path (same decode kernel; only the 3d operands differ)."""
+    d = load_golden(fname)
+    qa, qr, ck, pe, wuv = _ins(d)
+    packed = mcc.pack_uv_weights(wuv)
+    assert packed.buf.dtype == torch.bfloat16 and packed.buf.numel() == wuv.numel()
+    out = mcc.mla_attention_packed(qa, qr, ck, pe, packed, mc.SCALE)
+    assert out.dtype == torch.float32 and not torch.isnan(out).any()
+    assert rel_l2(sampled(out, d["out64_idx"]), d["out64_val"]) < TOL
+    ref = mcc.mla_attention_ex(qa, qr, ck, pe, wuv, mc.SCALE, precision="tensor")
+    assert rel_l2(out, ref) < 1e-2
+
+
+def test_packed_uv_attention_causal_and_rejects(mcc):
+    """Causal multi-query decode through the packed path against the oracle;
+    16-bit operands are rejected (the packing is for fp32 storage)."""
+    qa, qr, ck, pe, wuv = (t.to(DEV) for t in mc.attention_inputs(2, 3, 700, seed=41))
+    packed = mcc.pack_uv_weights(wuv)
+    out = mcc.mla_attention_packed(qa, qr, ck, pe, packed, mc.SCALE, causal=True)
+    ref = orc.mla_attention(*(t.double().cpu() for t in (qa, qr, ck, pe, wuv)), mc.SCALE, True)
+    assert rel_l2(out.cpu(), ref) < TOL
+    with pytest.raises((RuntimeError, ValueError)):
+        mcc.pack_uv_weights(wuv.to(torch.bfloat16))
+    with pytest.raises((RuntimeError, ValueError)):
+        mcc.mla_attention_packed(qa.half(), qr.half(), ck.half(), pe.half(), packed, mc.SCALE)
