@@ -123,6 +123,24 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
         : "memory");
 }
 
+// 3-D tiled store of the box at {x, y, z} from CTA-local shared memory (bulk
+// group completion). Coordinates are never negative here; elements outside the
+// tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int32_t x, int32_t y, int32_t z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];"
+                 ::"l"(tmap), "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory source of all but the newest N bulk groups has been read
+template <int N> __device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// all but the newest N bulk groups have completed (writes done)
+template <int N> __device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // ------------------------------------------------------------------ cluster
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

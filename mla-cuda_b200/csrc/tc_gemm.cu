@@ -368,11 +368,14 @@ __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
 // (N tile fastest, then M tile, then launch index z). The shared-memory ring runs
 // on across units, and the accumulator is double-buffered in TMEM (2 x BN
 // columns), so the epilogue of one unit overlaps the loads and MMAs of the next.
-template <int BN> constexpr int pstages() { return BN == 256 ? 4 : BN == 192 ? 5 : 6; }
+template <int BN> constexpr int pstages() { return BN == 256 ? 4 : BN == 192 ? 4 : 6; }
+// fp32 output tiles leave through shared memory: two 128-row x 32-column fp32
+// staging buffers (128B-swizzled), each stored by one TMA bulk tensor store
+constexpr int kCStageBytes = 128 * 32 * 4;
 // TMEM allocations are powers of two: two 192-column accumulators take 512 columns
 template <int BN> constexpr uint32_t ptmem_cols() { return BN == 192 ? 512u : 2u * BN; }
 template <int BN> constexpr size_t psmem_bytes() {
-    return 1024 + size_t(pstages<BN>()) * (a_bytes() + b_bytes<BN>()) + 256;
+    return 1024 + size_t(pstages<BN>()) * (a_bytes() + b_bytes<BN>()) + 2 * kCStageBytes + 256;
 }
 
 struct Units {
@@ -382,7 +385,8 @@ struct Units {
 template <typename T, int BN>
 __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Run r, const Units U,
-    const __grid_constant__ GemmRopeEpilogue re, const int use_re)
+    const __grid_constant__ GemmRopeEpilogue re, const int use_re, const __grid_constant__ CUtensorMap tmC,
+    const int use_tma_c)
 {
     constexpr int S = pstages<BN>();
     constexpr int BK = tc_gemm_bk<T>();
@@ -392,7 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
     static_assert(kStage % 1024 == 0, "stages stay 1024-byte aligned (128B swizzle)");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * kStage);
+    unsigned char* cstage = smem + S * kStage;   // [2][kCStageBytes], 1024-aligned
+    uint64_t* full = reinterpret_cast<uint64_t*>(cstage + 2 * kCStageBytes);
     uint64_t* empty = full + S;
     uint64_t* acc_full = empty + S;     // [2]
     uint64_t* acc_empty = acc_full + 2; // [2]
@@ -429,6 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
     if (warp == 0 && lane == 0) {
         tma_prefetch_desc(&tmA);
         tma_prefetch_desc(&tmB);
+        if (use_tma_c) tma_prefetch_desc(&tmC);
     }
     tc_fence_before();
     __syncthreads();
@@ -504,6 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
         const int q = warp & 3;
         const int row = q * 32 + lane;
         const uint32_t lane_off = uint32_t(q * 32) << 16;
+        const bool leader = threadIdx.x == 64;   // issues the output TMA stores
+        uint32_t chunk = 0;                      // staging-buffer sequence
         int64_t lt = 0;
         for (int64_t u = blockIdx.x; u < U.total; u += gridDim.x, ++lt) {
             int z; int64_t m0, n0, kb, nkb;
@@ -523,6 +531,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
                     for (int e = 0; e < 32; ++e) v[e] = 0u;
                 }
                 const int64_t n = n0 + c * 32;
+                if (use_tma_c) {
+                    // stage the 128 x 32 chunk (row = thread, 128B swizzle), then one
+                    // TMA store; the buffer is rewritten two chunks later, once that
+                    // store has read it
+                    if (n >= r.N) continue;                       // same for every thread
+                    unsigned char* sb = cstage + (chunk & 1u) * kCStageBytes;
+                    if (leader) bulk_wait_read<1>();
+                    named_bar_sync(1, 128);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        *reinterpret_cast<uint4*>(sb + row * 128 + ((u ^ (row & 7)) << 4)) =
+                            make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 128);
+                    if (leader) {
+                        tma_store_3d(&tmC, sb, int32_t(n), int32_t(z), int32_t(m0));
+                        bulk_commit();
+                    }
+                    ++chunk;
+                    continue;
+                }
                 if (m >= r.M || n >= r.N) continue;
                 if (use_re) {   // 2a2 epilogue: split per head, RoPE on the rope part
                     const int64_t qk = re.nope + re.rope;
@@ -590,6 +619,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
             tc_fence_before();
             mbar_arrive(&acc_empty[buf]);
         }
+        if (leader && use_tma_c) bulk_wait<0>();   // the output is written before the CTA retires
     }
     tc_fence_before();
     __syncthreads();
@@ -623,7 +653,17 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
     const int64_t grid = U.total < sm_count() ? U.total : sm_count();
     GemmRopeEpilogue re{};
     if (g.rope_epi) re = *g.rope_epi;
-    launch_pdl(kern, dim3(unsigned(grid)), dim3(kThreads), smem, st, ta, tb, r, U, re, g.rope_epi ? 1 : 0);
+    // fp32 output: a map over C's (n, z, m) with box 32 x 1 x 128 for the TMA-store epilogue
+    CUtensorMap tc{};
+    int use_tma_c = 0;
+    if (!g.rope_epi && (!g.c_is_t || std::is_same<T, float>::value) && (reinterpret_cast<uintptr_t>(g.C) & 15) == 0) {
+        const int64_t cdims[3] = {g.N, g.Z, g.M};
+        const int64_t cld[2] = {g.c_ldz, g.c_ldm};
+        const uint32_t cbox[3] = {32u, 1u, 128u};
+        use_tma_c = make_map_3d<float>(&tc, g.C, cdims, cld, cbox, true) ? 1 : 0;
+    }
+    launch_pdl(kern, dim3(unsigned(grid)), dim3(kThreads), smem, st, ta, tb, r, U, re, g.rope_epi ? 1 : 0, tc,
+               use_tma_c);
     return check_launch("tensor-core GEMM (persistent)");
 }
 
