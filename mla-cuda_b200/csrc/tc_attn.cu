@@ -32,8 +32,9 @@
 // storage is converted to bf16 in shared memory after the TMA load, so HBM
 // traffic stays one read of the fp32 cache.
 //
-// Warp roles (640 threads): warp 0 TMA producer, warp 1 MMA issuer and TMEM
-// owner (warps 2-3 idle), warps 16-19 fp32->bf16 converters (fp32 storage only), warps
+// Warp roles (640 threads): warp 0 TMA producer, warp 1 score-MMA issuer and
+// TMEM owner, warp 2 P.V issuer (warp 3 idle), warps 16-19 fp32->bf16
+// converters (fp32 storage only), warps
 // 4-7 and 12-15 softmax (keys 0-31 / 32-63 of each tile), warps 8-11 exchange
 // (query loads, partial-score push to the peer). Thread i of a warpgroup <->
 // TMEM lane i <-> head i: a warp reaches only TMEM lanes 32*(warp%4)..+31.
@@ -160,7 +161,7 @@ struct Params {
     int* err;
     int* trace;         // debug only (MLA_TC_TRACE): per-CTA progress words in mapped host memory
     long long* prof;    // debug only (MLA_TC_PROFILE builds): [grid][kProfSlots] cycle counters
-    long long* tl;      // debug only (MLA_TC_TIMELINE builds): [2 CTAs][8 events][kTlTiles] clock64
+    long long* tl;      // debug only (MLA_TC_TIMELINE builds): [2 CTAs][kTlEvents][kTlTiles] clock64
     int64_t batch, sq, sk;
     int causal;
     float c_log2;       // log2(e) / scale
@@ -194,9 +195,10 @@ constexpr int kProfSlots = 26;
 // host when MLA_TC_TL is set): clock64 of eight pipeline events for the first
 // kTlTiles tiles of CTAs 0 and 1.
 constexpr int kTlTiles = 256;
+constexpr int kTlEvents = 10;
 #ifdef MLA_TC_TIMELINE
 #define MLA_TL(ev, i) do { if (p.tl && blockIdx.x < 2 && (i) < kTlTiles) \
-    p.tl[(blockIdx.x * 8 + (ev)) * kTlTiles + (i)] = clock64(); } while (0)
+    p.tl[(blockIdx.x * kTlEvents + (ev)) * kTlTiles + (i)] = clock64(); } while (0)
 #else
 #define MLA_TL(ev, i) do { } while (0)
 #endif
@@ -390,29 +392,75 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     tma_load_2d(dst + 4 * kChunkBytes, &tm_pe, &bars->full[sl], int32_t(rank * kRopeHalf), row);
                 }
             }
-        } else if (warp == 1) {
-            // ------------------------------------------------------------ MMA issuer
-            // Order per tile i: the score MMA S(i), then P.V of tile i-1. S(i) writes
-            // score buffer i%2, whose previous contents P(i-2) were consumed by
-            // P.V(i-2), issued one iteration earlier (tcgen05 MMAs of one thread run
-            // in issue order).
-            if (lane == 0) {
-                constexpr uint32_t idesc_s = instr_desc(Tr::kFmt, 128, NK, 0, 0);
-                constexpr uint32_t idesc_o = instr_desc(Tr::kFmt, 128, kHalf, 0, 1);
-                const uint32_t smem_slots = smem_u32(slots);
+        } else if (warp == 1 || warp == 2) {
+            // ------------------------------------------------------------ MMA issuers
+            // Two issuing threads, so neither waits behind the other's instructions:
+            // warp 1 issues the score MMAs S(i), warp 2 the P.V MMAs. A thread's
+            // commit tracks only its own MMAs, so the order between the two streams
+            // is explicit: S(i) writes score buffer i%2 only after P.V(i-2) has
+            // completed (o_done), since P(i-2) lives there, and after the exchange
+            // warps have read S(i-2) (s_read). P.V(i) is issued only after p_full(i),
+            // which follows the completion of S(i); its commit releases the slot.
+            constexpr uint32_t idesc_s = instr_desc(Tr::kFmt, 128, NK, 0, 0);
+            constexpr uint32_t idesc_o = instr_desc(Tr::kFmt, 128, kHalf, 0, 1);
+            const uint32_t smem_slots = smem_u32(slots);
+            if (warp == 1 && lane == 0) {
                 const uint64_t qd0 = smem_desc(smem_u32(qrope), 16, 512, 4);
                 TileIter it = locate(p, t_begin);
                 int64_t seg = 0;
-                bool ok = true;
-                bool prev_first = false;
+                for (int64_t i = 0; i < n; ++i, advance(p, it)) {
+                    MLA_TL(9, i);
+                    const bool first = (i == 0) || it.j == 0;
+                    if (first) {
+                        if (!MLA_TW(4, mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4))) break;
+                        ++seg;
+                    }
+                    const int sl = int(i % Tr::kSlots);
+                    trace_put(p, 1, i * 16 + 1);
+                    uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
+                    if (!MLA_TW(5, mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5))) break;
+                    const int sb = int(i % kSBufs);
+                    if (i >= kSBufs) {
+                        // the exchange warps have read my partial of tile i-2, and P.V(i-2)
+                        // has consumed P(i-2), from this buffer
+                        const uint32_t par = uint32_t(((i - kSBufs) / kSBufs) & 1);
+                        if (!MLA_TW(13, mbar_wait(&bars->s_read[sb], par, abort, p.err, ERR_TIMEOUT_BASE + 13)) ||
+                            !MLA_TW(25, mbar_wait(&bars->o_done[sb], par, abort, p.err, ERR_TIMEOUT_BASE + 25)))
+                            break;
+                    }
+                    tc_fence_after();
+                    const uint32_t base = smem_slots + sl * kSlotBytes;
+                    // B = K [64 keys x 16 dims], K-major: latent chunk k/4 (128B swizzle,
+                    // +32 B per k-step), then the rope chunk (64B swizzle, +32 B per
+                    // k-step) against the rope query slice in shared memory.
+                    MLA_PROF(const long long t_si = clock64();)
+                    MLA_TL(8, i);
+                    const uint64_t bd0 = smem_desc(base, 16, 1024, 2);
+                    const uint64_t rd0 = smem_desc(base + 4 * kChunkBytes, 16, 512, 4);
+                    const uint32_t d_s = tmem + kTmemS + sb * NK;
+#pragma unroll
+                    for (int k = 0; k < kHalf / 16; ++k)
+                        mma_ts(d_s, tmem + kTmemQ + k * 8,
+                               bd0 + uint64_t(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4), idesc_s, k > 0 ? 1u : 0u);
+#pragma unroll
+                    for (int k = 0; k < kRopeHalf / 16; ++k)
+                        mma_ss(d_s, qd0 + uint64_t((k * 32) >> 4), rd0 + uint64_t((k * 32) >> 4), idesc_s, 1u);
+                    mma_commit(&bars->s_full[sb]);
+                    MLA_TL(0, i);
+                    MLA_PROF(wacc[16] += clock64() - t_si;)
+                    trace_put(p, 1, i * 16 + 2);
+                }
+            } else if (warp == 2 && lane == 0) {
                 // P.V of tile i: O += P(i) . V(i) (M = 128 heads, N = 256 latent dims,
                 // K = 64 keys), A = P from TMEM, B = the key tile's latent half,
                 // MN-major, 128B swizzle (LBO = stride between 64-dim chunks, SBO =
                 // stride between 8-key groups). Releases the slot, signals o_done.
-                auto issue_pv = [&](int64_t i, bool first) -> bool {
+                TileIter it = locate(p, t_begin);
+                for (int64_t i = 0; i < n; ++i, advance(p, it)) {
+                    const bool first = (i == 0) || it.j == 0;
                     const int sb = int(i % kSBufs);
                     if (!MLA_TW(3, mbar_wait(&bars->p_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err, ERR_TIMEOUT_BASE + 3)))
-                        return false;
+                        break;
                     tc_fence_after();
                     MLA_TL(6, i);
                     MLA_PROF(const long long t_pv = clock64();)
@@ -434,48 +482,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     mma_commit(&bars->o_done[sb]);
                     MLA_TL(1, i);
                     MLA_PROF(wacc[17] += clock64() - t_pv;)
-                    return true;
-                };
-                for (int64_t i = 0; i < n && ok; ++i) {
-                    const bool first = (i == 0) || it.j == 0;
-                    if (first) {
-                        if (!MLA_TW(4, mbar_wait(&bars->q_ready, uint32_t(seg & 1), abort, p.err, ERR_TIMEOUT_BASE + 4))) break;
-                        ++seg;
-                    }
-                    const int sl = int(i % Tr::kSlots);
-                    trace_put(p, 1, i * 16 + 1);
-                    uint64_t* fb = Tr::kConvert ? &bars->bf_full[sl] : &bars->full[sl];
-                    if (!MLA_TW(5, mbar_wait(fb, uint32_t((i / Tr::kSlots) & 1), abort, p.err, ERR_TIMEOUT_BASE + 5))) break;
-                    const int sb = int(i % kSBufs);
-                    // the exchange warps have read my partial of tile i-2 from this buffer
-                    if (i >= kSBufs && !MLA_TW(13, mbar_wait(&bars->s_read[sb], uint32_t(((i - kSBufs) / kSBufs) & 1),
-                                                            abort, p.err, ERR_TIMEOUT_BASE + 13)))
-                        break;
-                    tc_fence_after();
-                    const uint32_t base = smem_slots + sl * kSlotBytes;
-                    // B = K [64 keys x 16 dims], K-major: latent chunk k/4 (128B swizzle,
-                    // +32 B per k-step), then the rope chunk (64B swizzle, +32 B per
-                    // k-step) against the rope query slice in shared memory.
-                    MLA_PROF(const long long t_si = clock64();)
-                    const uint64_t bd0 = smem_desc(base, 16, 1024, 2);
-                    const uint64_t rd0 = smem_desc(base + 4 * kChunkBytes, 16, 512, 4);
-                    const uint32_t d_s = tmem + kTmemS + sb * NK;
-#pragma unroll
-                    for (int k = 0; k < kHalf / 16; ++k)
-                        mma_ts(d_s, tmem + kTmemQ + k * 8,
-                               bd0 + uint64_t(((k >> 2) * kChunkBytes + (k & 3) * 32) >> 4), idesc_s, k > 0 ? 1u : 0u);
-#pragma unroll
-                    for (int k = 0; k < kRopeHalf / 16; ++k)
-                        mma_ss(d_s, qd0 + uint64_t((k * 32) >> 4), rd0 + uint64_t((k * 32) >> 4), idesc_s, 1u);
-                    mma_commit(&bars->s_full[sb]);
-                    MLA_TL(0, i);
-                    MLA_PROF(wacc[16] += clock64() - t_si;)
-                    trace_put(p, 1, i * 16 + 2);
-                    if (i >= 1) ok = issue_pv(i - 1, prev_first);
-                    prev_first = first;
-                    advance(p, it);
                 }
-                if (ok && n > 0) issue_pv(n - 1, prev_first);
             }
         } else if (warp >= 8 && warp < 12) {
             setmaxnreg_dec<kRegExchange>();
@@ -1127,7 +1134,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
 #endif
 #ifdef MLA_TC_TIMELINE
         long long* tl_dev = nullptr;
-        const size_t tl_bytes = size_t(2) * 8 * kTlTiles * sizeof(long long);
+        const size_t tl_bytes = size_t(2) * kTlEvents * kTlTiles * sizeof(long long);
         if (getenv("MLA_TC_TL") && cudaMalloc(&tl_dev, tl_bytes) == cudaSuccess) {
             cudaMemsetAsync(tl_dev, 0, tl_bytes, st);
             p.tl = tl_dev;
@@ -1138,15 +1145,20 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
         timing_mark(st, false);
 #ifdef MLA_TC_TIMELINE
         if (tl_dev) {
-            std::vector<long long> h(size_t(2) * 8 * kTlTiles);
+            std::vector<long long> h(size_t(2) * kTlEvents * kTlTiles);
             if (cudaMemcpyAsync(h.data(), tl_dev, tl_bytes, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
                 cudaStreamSynchronize(st) == cudaSuccess) {
                 const int64_t nt = std::min<int64_t>(pl.tiles_per_cluster, kTlTiles);
                 for (int c = 0; c < 2; ++c) {
-                    auto at = [&](int ev, int64_t i) { return double(h[(c * 8 + ev) * kTlTiles + i]); };
+                    auto at = [&](int ev, int64_t i) { return double(h[(c * kTlEvents + ev) * kTlTiles + i]); };
                     double d[10] = {0};
                     int cnt = 0;
+                    double e[4] = {0, 0, 0, 0};
                     for (int64_t i = 8; i + 3 < nt - 4; ++i, ++cnt) {
+                        e[2] += at(9, i + 2) - at(1, i);        // PV(i) issued -> next iteration starts
+                        e[3] += at(3, i) - at(1, i);            // exchange released S(i), relative to PV(i) issued
+                        e[0] += at(8, i + 2) - at(9, i + 2);    // iteration start -> S(i+2) issue starts (waits)
+                        e[1] += at(0, i + 2) - at(8, i + 2);    // S(i+2) issue (18 MMAs + commit)
                         d[0] += at(5, i + 1) - at(5, i);        // tile period (softmax p_full)
                         d[1] += at(5, i) - at(4, i);            // softmax: x_full seen -> p_full
                         d[2] += at(6, i) - at(5, i);            // p_full -> MMA sees it
@@ -1164,6 +1176,9 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
                                                  "softmax idle between tiles"};
                     fprintf(stderr, "[mla timeline] CTA %d, %d tiles: average cycles\n", c, cnt);
                     for (int k = 0; k < 10; ++k) fprintf(stderr, "  %-28s %9.0f\n", nm[k], cnt ? d[k] / cnt : 0.0);
+                    fprintf(stderr, "  %-28s %9.0f\n  %-28s %9.0f\n  %-28s %9.0f\n  %-28s %9.0f\n",
+                            "  of which loop step", cnt ? e[2] / cnt : 0.0, "  of which waits", cnt ? e[0] / cnt : 0.0,
+                            "  of which S issue", cnt ? e[1] / cnt : 0.0, "s_read(i) - PV(i) issued", cnt ? e[3] / cnt : 0.0);
                 }
             }
             cudaFree(tl_dev);
