@@ -29,7 +29,10 @@ template <bool S3> constexpr int kernel_threads() { return S3 ? 320 : kThreads; 
 // drained into the round-to-nearest running sum. Measured against fp64 on the
 // attention fixtures: 1 block per drain matches fp32 CPU accuracy (rel-L2 7e-7),
 // 2 blocks double the error, 4 blocks triple it.
-constexpr int kGroup = 1;
+#ifndef MLA_3XTF32_GROUP
+#define MLA_3XTF32_GROUP 1
+#endif
+constexpr int kGroup = MLA_3XTF32_GROUP;
 enum : int { ERR_TIMEOUT_BASE = 200 };
 
 struct Run {
