@@ -178,6 +178,21 @@ __device__ __forceinline__ int64_t group_keys(const Params& p, int64_t g) {
 __device__ __forceinline__ int64_t group_tiles(const Params& p, int64_t g) {
     return (group_keys(p, g) + NK - 1) / NK;
 }
+// sum of ceil(x / NK) over x = 1..n (n >= 0): with n = NK*m + r, NK*m(m+1)/2 + r(m+1)
+__device__ __forceinline__ int64_t ceil_sum(int64_t n) {
+    if (n <= 0) return 0;
+    const int64_t m = n / NK, r = n % NK;
+    return (NK / 2) * m * (m + 1) + r * (m + 1);
+}
+// Key tiles of queries 0..q-1 of one sequence, in closed form (query i has
+// sk - sq + 1 + i keys under causal masking, sk otherwise), so that locating a
+// tile costs O(log sq) rather than a walk over every query (prefill has
+// thousands).
+__device__ __forceinline__ int64_t tiles_before(const Params& p, int64_t q) {
+    if (!p.causal) return q * ((p.sk + NK - 1) / NK);
+    const int64_t a = p.sk - p.sq + 1;   // keys of query 0 (>= 1: causal needs sk >= sq)
+    return ceil_sum(a + q - 1) - ceil_sum(a - 1);
+}
 
 // Debug cycle accounting (compiled in with -DMLA_TC_PROFILE, printed by the host
 // when MLA_TC_PROF is set): clock64 cycles spent in each wait site (slot = the
@@ -213,20 +228,17 @@ struct TileIter {
 
 // Locates global tile index t: returns the group and the tile inside it.
 __device__ __forceinline__ TileIter locate(const Params& p, int64_t t) {
-    int64_t per_batch = 0;
-    for (int64_t q = 0; q < p.sq; ++q) per_batch += group_tiles(p, q);
+    const int64_t per_batch = tiles_before(p, p.sq);
     const int64_t b = t / per_batch;
-    int64_t r = t % per_batch;
-    int64_t q = 0;
-    while (true) {
-        const int64_t n = group_tiles(p, b * p.sq + q);
-        if (r < n) break;
-        r -= n;
-        ++q;
+    const int64_t r = t % per_batch;
+    int64_t lo = 0, hi = p.sq - 1;   // the last query whose first tile is at or before r
+    while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) / 2;
+        if (tiles_before(p, mid) <= r) lo = mid; else hi = mid - 1;
     }
     TileIter it;
-    it.g = b * p.sq + q;
-    it.j = r;
+    it.g = b * p.sq + lo;
+    it.j = r - tiles_before(p, lo);
     it.keys = group_keys(p, it.g);
     it.tiles = (it.keys + NK - 1) / NK;
     return it;
@@ -937,11 +949,8 @@ __global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __re
     if (rowid >= groups * kHeads) return;
     const int64_t g = rowid / kHeads, h = rowid % kHeads;
     // first global tile of g
-    int64_t per_batch = 0;
-    for (int64_t q = 0; q < p.sq; ++q) per_batch += group_tiles(p, q);
     const int64_t b = g / p.sq, qg = g % p.sq;
-    int64_t t0 = b * per_batch;
-    for (int64_t q = 0; q < qg; ++q) t0 += group_tiles(p, b * p.sq + q);
+    const int64_t t0 = b * tiles_before(p, p.sq) + tiles_before(p, qg);
     const int64_t t1 = t0 + group_tiles(p, g);   // exclusive
     const int64_t c0 = t0 / p.tiles_per_cluster, c1 = (t1 - 1) / p.tiles_per_cluster;
     float M = -INFINITY;
