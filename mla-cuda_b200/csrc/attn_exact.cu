@@ -29,6 +29,7 @@
 #include "simt_gemm.cuh"
 #include "tc_gemm.cuh"
 
+#include <algorithm>
 #include <type_traits>
 
 namespace mla {
@@ -572,9 +573,56 @@ mla_status_t attn_exact_t3(const AArgs& a, cudaStream_t st) {
 
 }  // namespace
 
+// Problems past the tensor-core path's 2^31 score limit (long prefill) run it per
+// sequence and per block of queries. Under causal masking a query block
+// [q0, q1) needs only the keys its last query sees, Sk - (Sq - q1), so each block
+// is an ordinary smaller problem on the same cache rows.
+struct T3Chunks {
+    int64_t rows;   // queries per call
+    bool on;
+};
+T3Chunks t3_chunks(const AArgs& a) {
+    T3Chunks c{0, false};
+    if (t3_supported(a)) return c;
+    AArgs one = a;
+    one.batch = 1;
+    one.sq = 1;
+    if (!t3_supported(one)) return c;
+    const int64_t fit = ((int64_t(1) << 31) - 1) / (a.heads * a.sk);   // queries per call under the limit
+    const int64_t n = ceil_div(a.sq, fit);
+    c.rows = ceil_div(a.sq, n);
+    c.on = true;
+    return c;
+}
+AArgs t3_chunk_args(const AArgs& a, int64_t b, int64_t q0, int64_t rows) {
+    AArgs c = a;
+    const int64_t q1 = q0 + rows;
+    c.batch = 1;
+    c.sq = rows;
+    c.sk = a.causal ? a.sk - (a.sq - q1) : a.sk;
+    const int64_t row0 = b * a.sq + q0;   // first (sequence, query) row of the block
+    const size_t es = sizeof(float);
+    c.q_absorbed = static_cast<const char*>(a.q_absorbed) + size_t(row0 * a.heads * a.kv_rank) * es;
+    c.q_rope = static_cast<const char*>(a.q_rope) + size_t(row0 * a.heads * a.rope) * es;
+    c.c_kv = static_cast<const char*>(a.c_kv) + size_t(b * a.sk * a.kv_rank) * es;
+    c.pe_cache = static_cast<const char*>(a.pe_cache) + size_t(b * a.sk * a.rope) * es;
+    c.out = static_cast<char*>(a.out) + size_t(row0 * a.heads * a.v_dim) * es;
+    c.lse = a.lse ? a.lse + row0 * a.heads : nullptr;
+    return c;
+}
+
 template <typename T>
 size_t attn_exact_workspace(const AArgs& a) {
     if (std::is_same<T, float>::value && t3_supported(a)) return make_t3plan(a).total;
+    if (std::is_same<T, float>::value) {
+        const T3Chunks ch = t3_chunks(a);
+        if (ch.on) {
+            AArgs c = a;
+            c.batch = 1;
+            c.sq = ch.rows;
+            return make_t3plan(c).total;   // the largest block (all keys)
+        }
+    }
     return make_plan<T>(a).total;
 }
 
@@ -582,6 +630,15 @@ template <typename T>
 mla_status_t attn_exact(const AArgs& a, cudaStream_t st) {
     using Acc = acc_t<T>;
     if (std::is_same<T, float>::value && t3_supported(a)) return attn_exact_t3(a, st);
+    if (std::is_same<T, float>::value) {
+        const T3Chunks ch = t3_chunks(a);
+        if (ch.on) {
+            for (int64_t b = 0; b < a.batch; ++b)
+                for (int64_t q0 = 0; q0 < a.sq; q0 += ch.rows)
+                    MLA_TRY(attn_exact_t3(t3_chunk_args(a, b, q0, std::min(ch.rows, a.sq - q0)), st));
+            return MLA_OK;
+        }
+    }
     const APlan p = make_plan<T>(a);
     char* ws = static_cast<char*>(a.workspace);
     Acc* S = reinterpret_cast<Acc*>(ws + p.off_S);

@@ -145,3 +145,24 @@ def test_runs_on_the_current_stream(mcc):
         out = mcc.mla_attention(*ins, mc.SCALE)
     s.synchronize()
     assert torch.equal(out, ref)   # deterministic: no atomics on this path
+
+
+def test_exact_fp32_past_the_score_limit_causal(mcc):
+    """B*Sq*H*Sk above 2^31 (long causal prefill): the exact fp32 attention runs
+    per block of queries, each on the keys its last query sees. Rows on both
+    sides of the block boundary match the oracle (each row against its own
+    visible keys)."""
+    B, Sq, Sk = 1, 4096, 4200
+    assert B * Sq * 128 * Sk >= 2 ** 31
+    qa, qr, ck, pe, wuv = (t.to(DEV) for t in mc.attention_inputs(B, Sq, Sk, seed=17))
+    out = mcc.mla_attention_ex(qa, qr, ck, pe, wuv, mc.SCALE, causal=True, precision="exact")
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    for q in (0, 2047, 2048, Sq - 1):
+        keys = Sk - Sq + q + 1
+        args = [qa[:, q:q + 1].cpu(), qr[:, q:q + 1].cpu(), ck[:, :keys].cpu(), pe[:, :keys].cpu(), wuv.cpu()]
+        ref32 = orc.mla_attention(*args, mc.SCALE, False)
+        ref64 = orc.mla_attention(*(a.double() for a in args), mc.SCALE, False)
+        got = out[:, q:q + 1].cpu()
+        assert rel_l2(got, ref32) < 1e-5
+        assert rel_l2(got.double(), ref64) < 5 * max(rel_l2(ref32.double(), ref64), 1e-7)
