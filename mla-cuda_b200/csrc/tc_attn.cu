@@ -70,6 +70,7 @@ constexpr int kRope = 64;
 constexpr int kHalf = 256;                  // latent dims per CTA
 constexpr int kRopeHalf = 32;               // rope dims per CTA
 constexpr int kThreads = 640;
+constexpr int kQPrefetchTiles = 4;          // L2 prefetch of the next group's query, tiles ahead
 // Registers per thread at launch. The per-warpgroup split below (setmaxnreg)
 // is computed from it, and an increase waits until other warpgroups have
 // released enough, so the host refuses to launch if the compiled kernel does
@@ -156,7 +157,7 @@ static_assert(smem_bytes<float>() <= 232448 && smem_bytes<__nv_bfloat16>() <= 23
 struct Params {
     const void* qa;     // [B*Sq*H, 512]
     const void* qr;     // [B*Sq*H, 64]
-    float* O_part;      // [slots, 128, 512]
+    float* O_part;      // [slots][128 chunks of 4 dims][128 heads][4]: chunk-major, see the epilogue
     float* ml;          // [slots, 128, 2]  (running max in log2 units, sum)
     int* err;
     int* trace;         // debug only (MLA_TC_TRACE): per-CTA progress words in mapped host memory
@@ -210,7 +211,7 @@ constexpr int kProfSlots = 26;
 // host when MLA_TC_TL is set): clock64 of eight pipeline events for the first
 // kTlTiles tiles of CTAs 0 and 1.
 constexpr int kTlTiles = 256;
-constexpr int kTlEvents = 10;
+constexpr int kTlEvents = 12;
 #ifdef MLA_TC_TIMELINE
 #define MLA_TL(ev, i) do { if (p.tl && blockIdx.x < 2 && (i) < kTlTiles) \
     p.tl[(blockIdx.x * kTlEvents + (ev)) * kTlTiles + (i)] = clock64(); } while (0)
@@ -519,6 +520,20 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                 MLA_PROF(const long long t_pr = clock64();)
                 const bool first = (i == 0) || itp.j == 0;
                 const int sb = int(i % kSBufs);
+                // A few tiles before this group ends, pull my row of the next group's
+                // query into L2, so that loading it at the switch does not wait on
+                // DRAM round trips (the switch otherwise costs ~10 tile periods).
+                if (itp.j == (itp.tiles > kQPrefetchTiles ? itp.tiles - kQPrefetchTiles : 0) &&
+                    i + (itp.tiles - itp.j) < n) {
+                    const int64_t gnext = itp.g + 1;
+                    const char* qa_n = reinterpret_cast<const char*>(static_cast<const T*>(p.qa) +
+                                                                     (gnext * kHeads + row) * kRank + rank * kHalf);
+                    const char* qr_n = reinterpret_cast<const char*>(static_cast<const T*>(p.qr) +
+                                                                     (gnext * kHeads + row) * kRope + rank * kRopeHalf);
+#pragma unroll
+                    for (int l = 0; l < int(kHalf * sizeof(T)) / 128; ++l) prefetch_l2(qa_n + l * 128);
+                    prefetch_l2(qr_n);
+                }
                 if (first) {
                     // query of this group: the latent slice into TMEM as bf16/fp16
                     // pairs (32 dims = 16 TMEM columns per step, all 16-byte loads
@@ -569,6 +584,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     fence_proxy_async_smem();   // the rope slice is read by the tensor cores (async proxy)
                     tc_fence_before();
                     mbar_arrive(&bars->q_ready);
+                    if (warp == 8 && lane == 0) MLA_TL(10, i);
                 }
                 // every lane polls, then the warp reconverges: tcgen05.ld is warp-collective
                 if (!__all_sync(0xffffffffu, MLA_TW(6, mbar_wait(&bars->s_full[sb], uint32_t((i / kSBufs) & 1), abort, p.err,
@@ -814,16 +830,22 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                         break;
                     tc_fence_after();
                     const int64_t slot = cl * p.max_segs + seg_local;
-                    float* dst = p.O_part + (slot * kHeads + row) * kRank + rank * kHalf + hk * (kHalf / 2);
+                    // chunk-major partial output: the 4 dims of chunk ch (dims 4ch..4ch+3) of
+                    // head `row` at float4 index ch*128 + row of the slot, so that a warp's 32
+                    // rows store 512 contiguous bytes per instruction (a row-per-thread layout
+                    // put 32 cache lines into every store and slowed the next group's query
+                    // loads at a segment switch)
+                    float4* dst = reinterpret_cast<float4*>(p.O_part) + slot * (kRank / 4) * kHeads + row;
+                    const int ch0 = (rank * kHalf + hk * (kHalf / 2)) / 4;
 #pragma unroll 1
                     for (int c32 = 0; c32 < kHalf / 64; ++c32) {
                         uint32_t o[32];
                         tmem_ld32(tmem + lane_off + kTmemO + hk * (kHalf / 2) + c32 * 32, o);
                         tmem_ld_wait();
-                        float4* d4 = reinterpret_cast<float4*>(dst + c32 * 32);
                         for (int e = 0; e < 8; ++e)
-                            d4[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
-                                                __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+                            dst[(ch0 + c32 * 8 + e) * kHeads] =
+                                make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                            __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
                     }
                     // the row sum is the sum of the two halves' sums
                     bars->xl[hk * kHeads + row] = l_run;
@@ -834,6 +856,7 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
                     }
                     tc_fence_before();
                     ++seg_local;
+                    if (warp == 4 && lane == 0) MLA_TL(11, i);
                 }
                 advance(p, it);
             }
@@ -937,44 +960,64 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
 }
 
 // Combine the segments of every (group, head) row into a normalised context.
-// One warp per row; the cluster segments covering group g are contiguous.
+// One CTA per (group, 32-dim piece), one thread per head: each reads its row's
+// piece from every segment of the group (the cluster segments covering a group
+// are contiguous), chunk-major so that a warp's reads are contiguous, and the
+// result goes out through shared memory so that rows are written contiguously.
+constexpr int kCombinePiece = 32;
 template <typename OutT>
-__global__ void __launch_bounds__(256) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups,
-                                                      float* __restrict__ lse)
+__global__ void __launch_bounds__(kHeads) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups,
+                                                         float* __restrict__ lse)
 {
     pdl_wait();
     pdl_trigger();
-    const int64_t rowid = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (rowid >= groups * kHeads) return;
-    const int64_t g = rowid / kHeads, h = rowid % kHeads;
-    // first global tile of g
+    __shared__ float tile[kHeads][kCombinePiece + 1];
+    constexpr int kPieces = kRank / kCombinePiece;
+    const int64_t g = blockIdx.x / kPieces;
+    const int piece = int(blockIdx.x % kPieces);
+    const int h = threadIdx.x;
+    if (g >= groups) return;
     const int64_t b = g / p.sq, qg = g % p.sq;
-    const int64_t t0 = b * tiles_before(p, p.sq) + tiles_before(p, qg);
-    const int64_t t1 = t0 + group_tiles(p, g);   // exclusive
+    const int64_t t0 = b * tiles_before(p, p.sq) + tiles_before(p, qg);   // first global tile of g
+    const int64_t t1 = t0 + group_tiles(p, g);                            // exclusive
     const int64_t c0 = t0 / p.tiles_per_cluster, c1 = (t1 - 1) / p.tiles_per_cluster;
     float M = -INFINITY;
     for (int64_t c = c0; c <= c1; ++c) {
-        const int64_t g0 = locate(p, c * p.tiles_per_cluster).g;
-        const int64_t slot = c * p.max_segs + (g - g0);
+        const int64_t slot = c * p.max_segs + (g - locate(p, c * p.tiles_per_cluster).g);
         M = fmaxf(M, p.ml[(slot * kHeads + h) * 2]);
     }
-    float acc[16];
-    for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+    float acc[kCombinePiece];
+#pragma unroll
+    for (int e = 0; e < kCombinePiece; ++e) acc[e] = 0.f;
     float L = 0.f;
     for (int64_t c = c0; c <= c1; ++c) {
-        const int64_t g0 = locate(p, c * p.tiles_per_cluster).g;
-        const int64_t slot = c * p.max_segs + (g - g0);
+        const int64_t slot = c * p.max_segs + (g - locate(p, c * p.tiles_per_cluster).g);
         const float w = exp2f(p.ml[(slot * kHeads + h) * 2] - M);
         L += w * p.ml[(slot * kHeads + h) * 2 + 1];
-        const float* src = p.O_part + (slot * kHeads + h) * kRank;
-        for (int e = 0; e < 16; ++e) acc[e] += w * src[e * 32 + lane];
+        const float4* src = reinterpret_cast<const float4*>(p.O_part) + slot * (kRank / 4) * kHeads +
+                            int64_t(piece * (kCombinePiece / 4)) * kHeads + h;
+#pragma unroll
+        for (int e = 0; e < kCombinePiece / 4; ++e) {
+            const float4 v = src[e * kHeads];
+            acc[4 * e] += w * v.x;
+            acc[4 * e + 1] += w * v.y;
+            acc[4 * e + 2] += w * v.z;
+            acc[4 * e + 3] += w * v.w;
+        }
     }
     const float inv = 1.f / L;
     // log-sum-exp of the row's scaled scores (M and log2(L) are in log2 units)
-    if (lse && lane == 0) lse[rowid] = (M + log2f(L)) * 0.69314718055994531f;
-    OutT* dst = O_norm + rowid * kRank;
-    for (int e = 0; e < 16; ++e) dst[e * 32 + lane] = cvt<OutT>(acc[e] * inv);
+    if (lse && piece == 0) lse[g * kHeads + h] = (M + log2f(L)) * 0.69314718055994531f;
+#pragma unroll
+    for (int e = 0; e < kCombinePiece; ++e) tile[h][e] = acc[e] * inv;
+    __syncthreads();
+    OutT* dst = O_norm + g * kHeads * kRank + piece * kCombinePiece;
+#pragma unroll 4
+    for (int k = 0; k < kCombinePiece; ++k) {   // 128 consecutive elements: 4 rows x 32 dims
+        const int idx = k * kHeads + h;
+        const int r = idx / kCombinePiece, col = idx % kCombinePiece;
+        dst[int64_t(r) * kRank + col] = cvt<OutT>(tile[r][col]);
+    }
 }
 
 // ---------------------------------------------------------------- host side
@@ -1185,6 +1228,19 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
                                                  "softmax idle between tiles"};
                     fprintf(stderr, "[mla timeline] CTA %d, %d tiles: average cycles\n", c, cnt);
                     for (int k = 0; k < 10; ++k) fprintf(stderr, "  %-28s %9.0f\n", nm[k], cnt ? d[k] / cnt : 0.0);
+                    {   // the largest gap between consecutive tiles (group switches show here)
+                        double mx = 0; int64_t at_i = 0;
+                        for (int64_t i = 1; i + 1 < nt; ++i)
+                            if (at(4, i + 1) - at(4, i) > mx) { mx = at(4, i + 1) - at(4, i); at_i = i; }
+                        fprintf(stderr, "  largest tile gap %.0f cycles after tile %lld\n", mx, (long long)at_i);
+                        const int64_t i = at_i;
+                        const double z = at(4, i);
+                        fprintf(stderr, "  switch (cycles from softmax(i) start): p_full(i) %.0f, epilogue done %.0f, "
+                                "push(i) done %.0f, q_ready(i+1) %.0f, S(i+1) issue start %.0f, S(i+1) issued %.0f, "
+                                "exch s_full(i+1) %.0f, push(i+1) done %.0f, softmax(i+1) start %.0f\n",
+                                at(5, i) - z, at(11, i) - z, at(3, i) - z, at(10, i + 1) - z, at(8, i + 1) - z,
+                                at(0, i + 1) - z, at(2, i + 1) - z, at(3, i + 1) - z, at(4, i + 1) - z);
+                    }
                     fprintf(stderr, "  %-28s %9.0f\n  %-28s %9.0f\n  %-28s %9.0f\n  %-28s %9.0f\n",
                             "  of which loop step", cnt ? e[2] / cnt : 0.0, "  of which waits", cnt ? e[0] / cnt : 0.0,
                             "  of which S issue", cnt ? e[1] / cnt : 0.0, "s_read(i) - PV(i) issued", cnt ? e[3] / cnt : 0.0);
@@ -1241,17 +1297,16 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);
         }
-        const int64_t rows_total = pl.groups * kHeads;
-        const unsigned cblocks = unsigned((rows_total * 32 + 255) / 256);
+        const unsigned cblocks = unsigned(pl.groups * (kRank / kCombinePiece));
         if (a.v_dim % 32 != 0) {   // W_uv projection on CUDA cores from an fp32 context
-            launch_pdl(combine_kernel<float>, dim3(cblocks), dim3(256), 0, st, p, O_norm, int64_t(pl.groups), a.lse);
+            launch_pdl(combine_kernel<float>, dim3(cblocks), dim3(kHeads), 0, st, p, O_norm, int64_t(pl.groups), a.lse);
             MLA_TRY(check_launch("segment combine"));
             return attn_out_normalized<T>(a, O_norm, st);
         }
         if constexpr (std::is_same<T, float>::value) {
             if (a.W_uv_bf16) {   // pre-packed W_uv: bf16 context, kind::f16 projection, fp32 output
                 __nv_bfloat16* ctx16 = reinterpret_cast<__nv_bfloat16*>(O_norm);
-                launch_pdl(combine_kernel<__nv_bfloat16>, dim3(cblocks), dim3(256), 0, st, p, ctx16,
+                launch_pdl(combine_kernel<__nv_bfloat16>, dim3(cblocks), dim3(kHeads), 0, st, p, ctx16,
                            int64_t(pl.groups), a.lse);
                 MLA_TRY(check_launch("segment combine"));
                 TcGemm g{};
@@ -1267,7 +1322,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
         }
         // context in the storage dtype, then out[:, h] = ctx[:, h] @ W_uv[h]^T on the tensor cores
         T* ctx = reinterpret_cast<T*>(O_norm);
-        launch_pdl(combine_kernel<T>, dim3(cblocks), dim3(256), 0, st, p, ctx, int64_t(pl.groups), a.lse);
+        launch_pdl(combine_kernel<T>, dim3(cblocks), dim3(kHeads), 0, st, p, ctx, int64_t(pl.groups), a.lse);
         MLA_TRY(check_launch("segment combine"));
         TcGemm g{};
         g.A = ctx; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;
