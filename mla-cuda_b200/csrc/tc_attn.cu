@@ -960,12 +960,13 @@ __global__ void __maxnreg__(kLaunchRegs) mla_decode_tc_kernel(
 }
 
 // Combine the segments of every (group, head) row into a normalised context.
-// One CTA per (group, 32-dim piece), one thread per head: each reads its row's
-// piece from every segment of the group (the cluster segments covering a group
-// are contiguous), chunk-major so that a warp's reads are contiguous, and the
-// result goes out through shared memory so that rows are written contiguously.
-constexpr int kCombinePiece = 32;
-template <typename OutT>
+// One CTA per (group, piece of P dims), one thread per head: each reads its
+// row's piece from every segment of the group (the cluster segments covering a
+// group are contiguous), chunk-major so that a warp's reads are contiguous, and
+// the result goes out through shared memory so that rows are written
+// contiguously. P (32 down to 4) is chosen by the host so that few groups (long
+// contexts, small batches) still spread over every SM.
+template <typename OutT, int kCombinePiece>
 __global__ void __launch_bounds__(kHeads) combine_kernel(const Params p, OutT* __restrict__ O_norm, int64_t groups,
                                                          float* __restrict__ lse)
 {
@@ -981,28 +982,40 @@ __global__ void __launch_bounds__(kHeads) combine_kernel(const Params p, OutT* _
     const int64_t t0 = b * tiles_before(p, p.sq) + tiles_before(p, qg);   // first global tile of g
     const int64_t t1 = t0 + group_tiles(p, g);                            // exclusive
     const int64_t c0 = t0 / p.tiles_per_cluster, c1 = (t1 - 1) / p.tiles_per_cluster;
-    float M = -INFINITY;
-    for (int64_t c = c0; c <= c1; ++c) {
-        const int64_t slot = c * p.max_segs + (g - locate(p, c * p.tiles_per_cluster).g);
-        M = fmaxf(M, p.ml[(slot * kHeads + h) * 2]);
-    }
+    // online merge over the segments, four at a time so that their loads are in
+    // flight together (a long context spreads one group over many clusters)
+    float M = -INFINITY, L = 0.f;
     float acc[kCombinePiece];
 #pragma unroll
     for (int e = 0; e < kCombinePiece; ++e) acc[e] = 0.f;
-    float L = 0.f;
-    for (int64_t c = c0; c <= c1; ++c) {
-        const int64_t slot = c * p.max_segs + (g - locate(p, c * p.tiles_per_cluster).g);
-        const float w = exp2f(p.ml[(slot * kHeads + h) * 2] - M);
-        L += w * p.ml[(slot * kHeads + h) * 2 + 1];
-        const float4* src = reinterpret_cast<const float4*>(p.O_part) + slot * (kRank / 4) * kHeads +
-                            int64_t(piece * (kCombinePiece / 4)) * kHeads + h;
+    for (int64_t c = c0; c <= c1; c += 4) {
+        float m[4], l[4];
+        float4 v[4][kCombinePiece / 4];
 #pragma unroll
-        for (int e = 0; e < kCombinePiece / 4; ++e) {
-            const float4 v = src[e * kHeads];
-            acc[4 * e] += w * v.x;
-            acc[4 * e + 1] += w * v.y;
-            acc[4 * e + 2] += w * v.z;
-            acc[4 * e + 3] += w * v.w;
+        for (int u = 0; u < 4; ++u) {
+            if (c + u > c1) { m[u] = -INFINITY; l[u] = 0.f; continue; }
+            const int64_t slot = (c + u) * p.max_segs + (g - locate(p, (c + u) * p.tiles_per_cluster).g);
+            m[u] = p.ml[(slot * kHeads + h) * 2];
+            l[u] = p.ml[(slot * kHeads + h) * 2 + 1];
+            const float4* src = reinterpret_cast<const float4*>(p.O_part) + slot * (kRank / 4) * kHeads +
+                                int64_t(piece * (kCombinePiece / 4)) * kHeads + h;
+#pragma unroll
+            for (int e = 0; e < kCombinePiece / 4; ++e) v[u][e] = src[e * kHeads];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (c + u > c1) break;
+            const float Mn = fmaxf(M, m[u]);     // finite: a segment has at least one key
+            const float sc = exp2f(M - Mn), w = exp2f(m[u] - Mn);
+            L = L * sc + w * l[u];
+#pragma unroll
+            for (int e = 0; e < kCombinePiece / 4; ++e) {
+                acc[4 * e] = acc[4 * e] * sc + w * v[u][e].x;
+                acc[4 * e + 1] = acc[4 * e + 1] * sc + w * v[u][e].y;
+                acc[4 * e + 2] = acc[4 * e + 2] * sc + w * v[u][e].z;
+                acc[4 * e + 3] = acc[4 * e + 3] * sc + w * v[u][e].w;
+            }
+            M = Mn;
         }
     }
     const float inv = 1.f / L;
@@ -1297,18 +1310,28 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
             if (!done) return set_error(MLA_ERR_CUDA, "MLA: tensor-core attention did not finish (trace printed)");
             cudaFreeHost(trace_host);
         }
-        const unsigned cblocks = unsigned(pl.groups * (kRank / kCombinePiece));
+        // combine piece width: the widest of 32 / 16 / 8 / 4 dims that gives two CTAs per SM
+        int piece = 32;
+        while (piece > 4 && pl.groups * (kRank / piece) < 2 * int64_t(sm_count())) piece /= 2;
+        const unsigned cblocks = unsigned(pl.groups * (kRank / piece));
+        auto combine = [&](auto out_tag, void* out) -> mla_status_t {
+            using OutT = decltype(out_tag);
+            OutT* o = static_cast<OutT*>(out);
+            const int64_t gs = pl.groups;
+            if (piece == 32) launch_pdl(combine_kernel<OutT, 32>, dim3(cblocks), dim3(kHeads), 0, st, p, o, gs, a.lse);
+            else if (piece == 16) launch_pdl(combine_kernel<OutT, 16>, dim3(cblocks), dim3(kHeads), 0, st, p, o, gs, a.lse);
+            else if (piece == 8) launch_pdl(combine_kernel<OutT, 8>, dim3(cblocks), dim3(kHeads), 0, st, p, o, gs, a.lse);
+            else launch_pdl(combine_kernel<OutT, 4>, dim3(cblocks), dim3(kHeads), 0, st, p, o, gs, a.lse);
+            return check_launch("segment combine");
+        };
         if (a.v_dim % 32 != 0) {   // W_uv projection on CUDA cores from an fp32 context
-            launch_pdl(combine_kernel<float>, dim3(cblocks), dim3(kHeads), 0, st, p, O_norm, int64_t(pl.groups), a.lse);
-            MLA_TRY(check_launch("segment combine"));
+            MLA_TRY(combine(float{}, O_norm));
             return attn_out_normalized<T>(a, O_norm, st);
         }
         if constexpr (std::is_same<T, float>::value) {
             if (a.W_uv_bf16) {   // pre-packed W_uv: bf16 context, kind::f16 projection, fp32 output
                 __nv_bfloat16* ctx16 = reinterpret_cast<__nv_bfloat16*>(O_norm);
-                launch_pdl(combine_kernel<__nv_bfloat16>, dim3(cblocks), dim3(kHeads), 0, st, p, ctx16,
-                           int64_t(pl.groups), a.lse);
-                MLA_TRY(check_launch("segment combine"));
+                MLA_TRY(combine(__nv_bfloat16{}, ctx16));
                 TcGemm g{};
                 g.A = ctx16; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;
                 g.a_ld[0] = kRank; g.a_ld[1] = int64_t(kHeads) * kRank;
@@ -1322,8 +1345,7 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
         }
         // context in the storage dtype, then out[:, h] = ctx[:, h] @ W_uv[h]^T on the tensor cores
         T* ctx = reinterpret_cast<T*>(O_norm);
-        launch_pdl(combine_kernel<T>, dim3(cblocks), dim3(kHeads), 0, st, p, ctx, int64_t(pl.groups), a.lse);
-        MLA_TRY(check_launch("segment combine"));
+        MLA_TRY(combine(T{}, ctx));
         TcGemm g{};
         g.A = ctx; g.a_dims[0] = kRank; g.a_dims[1] = kHeads; g.a_dims[2] = pl.groups;
         g.a_ld[0] = kRank; g.a_ld[1] = int64_t(kHeads) * kRank;
