@@ -371,14 +371,21 @@ __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
 // (N tile fastest, then M tile, then launch index z). The shared-memory ring runs
 // on across units, and the accumulator is double-buffered in TMEM (2 x BN
 // columns), so the epilogue of one unit overlaps the loads and MMAs of the next.
-template <int BN> constexpr int pstages() { return BN == 256 ? 4 : BN == 192 ? 4 : 6; }
+template <int BN> constexpr int pstages() { return BN == 256 ? 4 : BN == 192 ? 5 : 6; }
 // fp32 output tiles leave through shared memory: two 128-row x 32-column fp32
 // staging buffers (128B-swizzled), each stored by one TMA bulk tensor store
 constexpr int kCStageBytes = 128 * 32 * 4;
+// 192-column tiles serve only the RoPE epilogue (no fp32 C), so they keep no staging
+template <int BN> constexpr int cstage_bytes() { return BN == 192 ? 0 : 2 * kCStageBytes; }
+// RoPE epilogue: cos / sin of every (query, frequency) computed once per CTA
+// when the queries are few (decode: every row of a tile shares one position)
+constexpr int kRopeTabQ = 4;
+template <int BN> constexpr int ropetab_bytes() { return BN == 192 ? kRopeTabQ * 64 * 8 : 0; }
 // TMEM allocations are powers of two: two 192-column accumulators take 512 columns
 template <int BN> constexpr uint32_t ptmem_cols() { return BN == 192 ? 512u : 2u * BN; }
 template <int BN> constexpr size_t psmem_bytes() {
-    return 1024 + size_t(pstages<BN>()) * (a_bytes() + b_bytes<BN>()) + 2 * kCStageBytes + 256;
+    return 1024 + size_t(pstages<BN>()) * (a_bytes() + b_bytes<BN>()) + cstage_bytes<BN>() + ropetab_bytes<BN>() +
+           256;
 }
 
 struct Units {
@@ -399,8 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
     static_assert(kStage % 1024 == 0, "stages stay 1024-byte aligned (128B swizzle)");
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* cstage = smem + S * kStage;   // [2][kCStageBytes], 1024-aligned
-    uint64_t* full = reinterpret_cast<uint64_t*>(cstage + 2 * kCStageBytes);
+    unsigned char* cstage = smem + S * kStage;   // [2][kCStageBytes], 1024-aligned (not for BN 192)
+    // (cos, sin) of positions[q] * inv_freq[j], [kRopeTabQ][64] (192-column tiles only)
+    float2 (*rope_cs)[64] = reinterpret_cast<float2 (*)[64]>(cstage + cstage_bytes<BN>());
+    uint64_t* full = reinterpret_cast<uint64_t*>(cstage + cstage_bytes<BN>() + ropetab_bytes<BN>());
     uint64_t* empty = full + S;
     uint64_t* acc_full = empty + S;     // [2]
     uint64_t* acc_empty = acc_full + 2; // [2]
@@ -516,6 +525,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
         const bool leader = threadIdx.x == 64;   // issues the output TMA stores
         uint32_t chunk = 0;                      // staging-buffer sequence
         int64_t lt = 0;
+        const bool rope_tab = ropetab_bytes<BN>() > 0 && use_re && re.sq <= kRopeTabQ;
+        if (rope_tab) {
+            const int half = int(re.rope / 2);
+            for (int idx = threadIdx.x - 64; idx < int(re.sq) * half; idx += 128) {
+                const int qq = idx / half, j = idx % half;
+                const float ang = float(re.positions[qq]) * re.inv_freq[j];
+                rope_cs[qq][j] = make_float2(cosf(ang), sinf(ang));
+            }
+            named_bar_sync(1, 128);
+        }
         for (int64_t u = blockIdx.x; u < U.total; u += gridDim.x, ++lt) {
             int z; int64_t m0, n0, kb, nkb;
             unit(u, z, m0, n0, kb, nkb);
@@ -578,14 +597,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_gemm_persist_kernel(
                         }
                     } else {
                         const int64_t ro = o - re.nope;                 // first rope dim of this chunk
-                        const float pos = float(re.positions[m % re.sq]);
+                        const int64_t qq = m % re.sq;
+                        const float pos = float(re.positions[qq]);
                         float4* dst = reinterpret_cast<float4*>(re.q_rope + (m * re.heads + h) * re.rope + ro);
                         for (int e = 0; e < 8; ++e) {
                             float out[4];
                             for (int pp = 0; pp < 2; ++pp) {
                                 const int j = int(ro / 2) + 2 * e + pp;
-                                const float ang = pos * re.inv_freq[j];
-                                const float cs = cosf(ang), sn = sinf(ang);
+                                float cs, sn;
+                                if (rope_tab) {
+                                    const float2 t = rope_cs[qq][j];
+                                    cs = t.x;
+                                    sn = t.y;
+                                } else {
+                                    const float ang = pos * re.inv_freq[j];
+                                    cs = cosf(ang);
+                                    sn = sinf(ang);
+                                }
                                 const float ev = __uint_as_float(v[4 * e + 2 * pp]);
                                 const float od = __uint_as_float(v[4 * e + 2 * pp + 1]);
                                 out[2 * pp] = ev * cs - od * sn;
@@ -659,7 +687,8 @@ mla_status_t launch_persist(const TcGemm& g, cudaStream_t st) {
     // fp32 output: a map over C's (n, z, m) with box 32 x 1 x 128 for the TMA-store epilogue
     CUtensorMap tc{};
     int use_tma_c = 0;
-    if (!g.rope_epi && (!g.c_is_t || std::is_same<T, float>::value) && (reinterpret_cast<uintptr_t>(g.C) & 15) == 0) {
+    if (cstage_bytes<BN>() > 0 && !g.rope_epi && (!g.c_is_t || std::is_same<T, float>::value) &&
+        (reinterpret_cast<uintptr_t>(g.C) & 15) == 0) {
         const int64_t cdims[3] = {g.N, g.Z, g.M};
         const int64_t cld[2] = {g.c_ldz, g.c_ldm};
         const uint32_t cbox[3] = {32u, 1u, 128u};
