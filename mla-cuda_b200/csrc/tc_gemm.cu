@@ -68,7 +68,8 @@ template <int BN, bool S3> constexpr size_t smem_bytes() {
 template <typename T, int BN, bool S3>
 __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
     const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, const Run r)
+    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, const Run r,
+    const __grid_constant__ CUtensorMap tmC, const int use_tma_c)
 {
     constexpr int S = stages<BN, S3>();
     constexpr int BK = tc_gemm_bk<T>();             // elements per 128-byte row
@@ -312,6 +313,7 @@ __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
         }
         if (ok) {
             float rmax = -__int_as_float(0x7f800000);
+            const bool leader = threadIdx.x == 64;   // issues the output TMA stores
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 if (nkb > 0) {
@@ -321,6 +323,30 @@ __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
                     for (int e = 0; e < 32; ++e) v[e] = 0u;
                 }
                 const int64_t n = n0 + c * 32;
+                if (use_tma_c) {
+                    // fp32 output through shared memory: every stage has been consumed
+                    // (the accumulator is final), so two 16 KB buffers at the start of the
+                    // stage area hold 128 x 32 chunks (row = thread, 128B swizzle), each
+                    // leaving in one TMA store; rows and columns outside C are clipped
+                    if (n >= r.N) continue;                       // same for every thread
+                    if (r.rowmax)
+                        for (int e = 0; e < 32; ++e)
+                            if (n + e < r.n_valid) rmax = fmaxf(rmax, __uint_as_float(v[e]));
+                    unsigned char* sbuf = smem + (c & 1) * (128 * 32 * 4);
+                    if (leader) bulk_wait_read<1>();
+                    named_bar_sync(1, 128);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        *reinterpret_cast<uint4*>(sbuf + row * 128 + ((u ^ (row & 7)) << 4)) =
+                            make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                    fence_proxy_async_smem();
+                    named_bar_sync(1, 128);
+                    if (leader) {
+                        tma_store_3d(&tmC, sbuf, int32_t(n), int32_t(z), int32_t(m0));
+                        bulk_commit();
+                    }
+                    continue;
+                }
                 if (m >= r.M || n >= r.N) continue;
                 const int64_t off = m * r.c_ldm + int64_t(z) * r.c_ldz + n;
                 if (!r.c_is_t || std::is_same<T, float>::value) {
@@ -353,6 +379,7 @@ __global__ void __launch_bounds__(kernel_threads<S3>(), 1) tc_gemm_kernel(
                 }
             }
             if (r.rowmax && m < r.M) r.rowmax[(int64_t(z) * r.M + m) * gridDim.x + blockIdx.x] = rmax;
+            if (leader && use_tma_c) bulk_wait<0>();   // the output is written before the CTA retires
         }
     }
     tc_fence_before();
@@ -723,7 +750,16 @@ mla_status_t launch(const TcGemm& g, cudaStream_t st) {
     const size_t smem = smem_bytes<BN, S3>();
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     dim3 grid(unsigned(ceil_div(g.N, BN)), unsigned(ceil_div(g.M, 128)), unsigned(g.Z));
-    kern<<<grid, kernel_threads<S3>(), smem, st>>>(ta, tb, ta2, tb2, r);
+    // fp32 output: TMA-store epilogue over C's (n, z, m) map (box 32 x 1 x 128)
+    CUtensorMap tc{};
+    int use_tma_c = 0;
+    if ((!g.c_is_t || std::is_same<T, float>::value) && (reinterpret_cast<uintptr_t>(g.C) & 15) == 0) {
+        const int64_t cdims[3] = {g.N, g.Z, g.M};
+        const int64_t cld[2] = {g.c_ldz, g.c_ldm};
+        const uint32_t cbox[3] = {32u, 1u, 128u};
+        use_tma_c = make_map_3d<float>(&tc, g.C, cdims, cld, cbox, true) ? 1 : 0;
+    }
+    kern<<<grid, kernel_threads<S3>(), smem, st>>>(ta, tb, ta2, tb2, r, tc, use_tma_c);
     return check_launch("tensor-core GEMM");
 }
 
