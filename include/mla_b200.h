@@ -65,7 +65,10 @@ typedef enum mla_dtype {
  *                   storage, fp32 otherwise), the reference's policy (AccType,
  *                   mla_kernels.cu:118-120). fp32 storage runs the contractions
  *                   on the tensor cores in 3xTF32 (fp32-class products, fp32
- *                   sums); other dtypes on CUDA cores. rel-L2 <= 1e-5 in fp32.
+ *                   sums); fp16 / bf16 storage on the tensor cores in kind::f16
+ *                   (16-bit products are exact in fp32, fp32 sums, the
+ *                   probabilities carried as a 16-bit head plus remainder);
+ *                   fp64 on CUDA cores. rel-L2 <= 1e-5 in fp32.
  *  MLA_PREC_TENSOR: tcgen05 tensor cores with bf16 operands and fp32
  *                   accumulation, scores never written to memory. fp32, fp16
  *                   and bf16 storage; rel-L2 <= 2e-2 against the fp32 path. */
