@@ -1313,6 +1313,10 @@ mla_status_t tc_attention(const AArgs& a, cudaStream_t st, bool exact) {
         // combine piece width: the widest of 32 / 16 / 8 / 4 dims that gives two CTAs per SM
         int piece = 32;
         while (piece > 4 && pl.groups * (kRank / piece) < 2 * int64_t(sm_count())) piece /= 2;
+        if (const char* e = getenv("MLA_COMBINE_PIECE")) {   // debug / tuning knob: 32, 16, 8 or 4
+            const int v = atoi(e);
+            if (v == 32 || v == 16 || v == 8 || v == 4) piece = v;
+        }
         const unsigned cblocks = unsigned(pl.groups * (kRank / piece));
         auto combine = [&](auto out_tag, void* out) -> mla_status_t {
             using OutT = decltype(out_tag);
