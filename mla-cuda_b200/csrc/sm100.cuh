@@ -50,13 +50,6 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-// Arrive on the barrier at the same offset in CTA `peer` of this cluster,
-// releasing this thread's prior (local and remote) writes at cluster scope.
-__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t peer) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(bar)), "r"(peer));
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
-}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -195,11 +188,6 @@ __device__ __forceinline__ uint32_t cluster_id_x() {
     asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
     return r;
 }
-__device__ __forceinline__ uint32_t nclusters_x() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-    return r;
-}
 // Per-warpgroup register budget changes (all warps of the warpgroup execute
 // them together). An increase waits until registers released by decreases in
 // other warpgroups of the CTA are available.
@@ -221,10 +209,6 @@ __device__ __forceinline__ uint32_t map_peer(const void* local, uint32_t peer) {
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(peer));
     return remote;
-}
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-                 : "memory");
 }
 
 // Asynchronous 16-byte store into a peer CTA's shared memory that counts its
@@ -353,20 +337,6 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
-}
-
-// bf16 round-to-nearest-even on the integer pipe (the XU pipe that cvt uses is
-// the decode kernel's scarcest unit): adding 0x7FFF plus the lowest kept bit
-// carries into bit 16 exactly when the discarded half is above one half ULP,
-// or equal to it with an odd kept part. Identical to cvt.rn.bf16.f32 for every
-// input except signalling NaNs whose payload sits only in the low 16 bits
-// (those become infinities).
-__device__ __forceinline__ uint32_t bf16_rn_hi(float x) {
-    const uint32_t u = __float_as_uint(x);
-    return u + 0x7FFFu + ((u >> 16) & 1u);   // bf16 bits in the upper half
-}
-__device__ __forceinline__ uint32_t pack_bf16_int(float lo, float hi) {
-    return __byte_perm(bf16_rn_hi(lo), bf16_rn_hi(hi), 0x7632);
 }
 
 __device__ __forceinline__ float ex2(float x) {
