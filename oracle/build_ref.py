@@ -21,7 +21,8 @@ OUT = HERE / "_ref"
 
 
 def build() -> Path:
-    ref = Path(os.environ.get("REFERENCE_DIR", "/root/reference"))
+    # default: a "reference" checkout beside this repository
+    ref = Path(os.environ.get("REFERENCE_DIR", str(HERE.parent.parent / "reference")))
     src = ref / "mla_kernels.cu"
     if not src.exists():
         raise FileNotFoundError(f"{src} not found (set REFERENCE_DIR)")
